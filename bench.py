@@ -1,0 +1,413 @@
+#!/usr/bin/env python3
+"""Benchmark: fused rANS decode + dequant + GEMV on B200.
+
+Workload (one GPU): the Llama-7B layer-shape GEMV sweep at batch 1 --
+[4096x4096], [11008x4096], [4096x11008] -- with discrete-Laplace (b = 0.5)
+4-bit symbols, group-128 fp16 scales U(0.01, 0.03), zero-point 8 and
+x ~ N(0, 1) fp16 (seeded synthetic inputs of the reference's benchmark
+shapes). Each matrix is encoded into the packed format (8x512 / 8x256 tiles,
+32 interleaved rANS streams per tile, one table per matrix). To keep every
+step's weights out of L2 (126 MB), REPLICAS copies of the three matrices
+(~180 MB compressed in total) sit in HBM and one step runs the sweep over
+all of them: 3 * REPLICAS fused GEMV launches, captured in a CUDA graph.
+
+Metric: effective 4-bit weight GB/s = (M*K/2 bytes per matrix) / time, the
+reference's "fused decode + GEMV" throughput view. The JSON line also
+carries the compressed-byte HBM view (roofline), symbols/s, an end-to-end
+figure through the public API with host buffers, and the reference CPU path
+(the oracle's restatement) timed on this host.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ecq|reference]
+
+With N > 1 (torchrun, one rank per GPU) every rank runs the same sweep on
+its own GPU (weak scaling; the tiles are independent, no collective).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008)]
+GROUP = 128
+LAPLACE_B = 0.5
+WORKLOAD = "llama7b_gemv_sweep_b1"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ecq", "reference"], default="ecq")
+    ap.add_argument("--replicas", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def make_inputs():
+    """Symbols, scales and x of the three shapes (seeded), plus their packed encodings."""
+    import ecq_b200 as ecq
+    from ecq_b200 import synthetic as syn
+
+    out = []
+    for i, (M, K) in enumerate(SHAPES):
+        sym = syn.laplace_symbols(M, K, b=LAPLACE_B, seed=10 * i)
+        sc = syn.group_scales(M, K, GROUP, seed=10 * i + 1)
+        x = syn.activations(1, K, seed=10 * i + 2)
+        enc = ecq.encode_matrix(sym, group_size=GROUP)
+        out.append(dict(M=M, K=K, sym=sym, scales=sc, x=x, enc=enc))
+    return out
+
+
+def algorithmic_bytes(enc, M, K, B=1):
+    """Bytes the fused GEMV must move: tile streams + per-tile offsets +
+    per-stream lengths + decode table (64 KB) + fp16 scales + x + y."""
+    ng = (K + GROUP - 1) // GROUP
+    return (enc.compressed_bytes + 4 * (enc.n_tiles + 1) + 2 * 32 * enc.n_tiles + 4 * 16384
+            + 2 * M * ng + 2 * B * K + 2 * B * M)
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "50", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [v.strip() for v in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(inputs, threads, repeats=2):
+    """The reference's CPU path (oracle restatement): per tile decode +
+    dequant + matvec, over all three matrices, on `threads` host threads."""
+    from oracle import oracle
+
+    best = None
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        for d in inputs:
+            e = d["enc"]
+            y, bad = oracle.gemv_packed(e.data, e.tile_offset, e.stream_len, d["M"], d["K"], 8, e.tile_cols,
+                                        e.table.freq, d["scales"].astype(np.float32), GROUP,
+                                        d["x"].astype(np.float32), threads=threads)
+            assert bad == 0
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    eff = sum(d["M"] * d["K"] / 2 for d in inputs)
+    return eff / best / 1e9, best
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle
+
+    inputs = make_inputs()
+    threads = oracle.cpu_count()
+    eff = sum(d["M"] * d["K"] / 2 for d in inputs)
+    # each step: the full sweep once (bounded: ~0.2-1 s on a many-core host)
+    for _ in range(max(args.warmup, 1)):
+        cpu_baseline(inputs, threads, repeats=1)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_baseline(inputs, threads, repeats=1)
+    dt = time.perf_counter() - t0
+    value = eff * args.steps / dt / 1e9
+    line = {
+        "impl": "reference", "metric": "fused decode+GEMV effective 4-bit weight GB/s", "value": round(value, 3),
+        "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * dt / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "shapes": SHAPES, "laplace_b": LAPLACE_B, "group_size": GROUP,
+                   "batch": 1, "replicas": 1},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": "one full sweep (3 matrices, 107M symbols) per step: oracle C restatement of "
+                                   "interleaved_rans_decode per tile + dequant + matvec, threads over row slabs"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ecq(args):
+    import torch
+    import torch.distributed as dist
+
+    import ecq_b200 as ecq
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    inputs = make_inputs()
+    R = args.replicas
+    sets = []
+    for r in range(R):
+        mats = []
+        for d in inputs:
+            m = ecq.DeviceMatrix.from_encoded(d["enc"], group_size=GROUP, device=dev)
+            mats.append(dict(m=m, sc=torch.from_numpy(d["scales"]).to(dev), x=torch.from_numpy(d["x"]).to(dev),
+                             y=torch.empty(1, d["M"], dtype=torch.float16, device=dev)))
+        sets.append(mats)
+    torch.cuda.synchronize()
+
+    # correctness gate before timing: every shape once against the oracle
+    from oracle import oracle
+
+    for d, e in zip(inputs, sets[0]):
+        y = e["m"].gemv(e["x"], e["sc"], out=e["y"])
+        e["m"].check()
+        yr = oracle.dequant_gemv(d["sym"], d["scales"].astype(np.float32), GROUP, d["x"].astype(np.float32))
+        err = float(np.max(np.abs(y.float().cpu().numpy()[0] - yr)) / np.max(np.abs(yr)))
+        assert err <= 2e-3, f"parity gate failed: {err}"
+
+    stream = torch.cuda.Stream(device=dev)
+    # one graph per step (the whole ring) and one graph per launch (for per-kernel timing)
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for mats in sets:  # warm the launch path (attributes) before capture
+            for e in mats:
+                e["m"].gemv(e["x"], e["sc"], out=e["y"])
+        stream.synchronize()
+        with torch.cuda.graph(step_graph, stream=stream):
+            for mats in sets:
+                for e in mats:
+                    e["m"].gemv(e["x"], e["sc"], out=e["y"])
+        launch_graphs = []
+        for mats in sets:
+            row = []
+            for e in mats:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    e["m"].gemv(e["x"], e["sc"], out=e["y"])
+                row.append(g)
+            launch_graphs.append(row)
+    launches_per_step = 3 * R
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step_graph.replay()
+    stream.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                step_graph.replay()
+            ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    eff_per_step = R * sum(d["M"] * d["K"] / 2 for d in inputs)
+    sym_per_step = R * sum(d["M"] * d["K"] for d in inputs)
+    value = world * eff_per_step * args.steps / (ms_max / 1e3) / 1e9
+
+    # per-launch durations (events around each single-launch graph, same ring order)
+    per_shape_ms = [[] for _ in SHAPES]
+    with torch.cuda.stream(stream):
+        evs = []
+        n_rounds = max(3, min(args.steps // 4, 50))
+        for _ in range(n_rounds):
+            for row in launch_graphs:
+                for i, g in enumerate(row):
+                    a = torch.cuda.Event(enable_timing=True)
+                    b = torch.cuda.Event(enable_timing=True)
+                    a.record(stream)
+                    g.replay()
+                    b.record(stream)
+                    evs.append((i, a, b))
+    stream.synchronize()
+    for i, a, b in evs:
+        per_shape_ms[i].append(a.elapsed_time(b))
+    avg_ms = [statistics.mean(v) for v in per_shape_ms]
+    share = [a * 1 for a in avg_ms]
+    dom = int(np.argmax(share))
+    d = inputs[dom]
+    alg = algorithmic_bytes(d["enc"], d["M"], d["K"])
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = alg / (avg_ms[dom] / 1e3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "gemv_dram_traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get(f"{d['M']}x{d['K']}")
+        except Exception:
+            traffic = None
+
+    # end to end through the public API: x from pinned host, fused GEMVs, y back to pinned host
+    e2e = None
+    if not args.no_e2e:
+        hx = [torch.from_numpy(d0["x"]).pin_memory() for d0 in inputs]
+        hy = [torch.empty(1, d0["M"], dtype=torch.float16).pin_memory() for d0 in inputs]
+        dx = [[torch.empty_like(h, device=dev) for h in hx] for _ in sets]
+        e2e_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(e2e_graph, stream=stream):
+                for si, mats in enumerate(sets):
+                    for i, e in enumerate(mats):
+                        dx[si][i].copy_(hx[i], non_blocking=True)
+                        e["m"].gemv(dx[si][i], e["sc"], out=e["y"])
+                        hy[i].copy_(e["y"], non_blocking=True)
+        e2e_steps = max(1, args.steps // 2)
+        with torch.cuda.stream(stream):
+            for _ in range(max(args.warmup, 3)):
+                e2e_graph.replay()
+                stream.synchronize()
+            barrier()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            a.record(stream)
+            for _ in range(e2e_steps):
+                e2e_graph.replay()
+                stream.synchronize()  # the host reads every step's results
+                _ = float(hy[0][0, 0])
+            b.record(stream)
+            b.synchronize()
+            wall = time.perf_counter() - t0
+        te = torch.tensor([max(a.elapsed_time(b), wall * 1e3)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e_ms = float(te.item())
+        h2d = R * sum(2 * d0["K"] for d0 in inputs)
+        d2h = R * sum(2 * d0["M"] for d0 in inputs)
+        e2e = {"value": round(world * eff_per_step * e2e_steps / (e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "DeviceMatrix.gemv (libecq C ABI) in a CUDA graph with pinned-host x/y copies; "
+                       "host reads y after every step"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as _o
+
+        threads = _o.cpu_count()
+        v, secs = cpu_baseline(inputs, threads, repeats=2)
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"one full sweep (3 matrices, {sum(d0['M'] * d0['K'] for d0 in inputs) / 1e6:.0f}M "
+                         f"symbols, {secs:.2f} s): oracle C restatement of interleaved_rans_decode per tile + "
+                         f"dequant + matvec, {threads} threads over row slabs"}
+
+    comp_bytes_step = R * sum(algorithmic_bytes(d0["enc"], d0["M"], d0["K"]) for d0 in inputs)
+    ms_step = ms_max / args.steps
+    line = {
+        "metric": "fused decode+GEMV effective 4-bit weight GB/s", "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "shapes": SHAPES, "laplace_b": LAPLACE_B, "group_size": GROUP,
+                   "batch": 1, "tile": "8x512 (K=4096) / 8x256 (K=11008), 32 streams",
+                   "replicas": R, "l2": f"inputs larger than L2: {R} replica sets, "
+                                         f"{comp_bytes_step / 1e6:.0f} MB per step > 126 MB",
+                   "bits_per_symbol": [round(d0["enc"].bits_per_symbol, 4) for d0 in inputs],
+                   "parallelism": f"replicas{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                     "kernel": f"matrix_kernel gemv {d['M']}x{d['K']}",
+                     "avg_launch_us": round(avg_ms[dom] * 1e3, 2), "algorithmic_bytes": alg,
+                     "per_shape_us": {f"{M}x{K}": round(v * 1e3, 2) for (M, K), v in zip(SHAPES, avg_ms)}},
+        "views": {
+            "effective_4bit_gbs": round(value / world, 2),
+            "compressed_gbs": round(comp_bytes_step / (ms_step / 1e3) / 1e9, 2),
+            "symbols_per_s": round(sym_per_step / (ms_step / 1e3), 1),
+            "plain_4bit_roofline_gbs": hbm_peak,
+        },
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        del step_graph, launch_graphs
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ecq(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,125 @@
+"""ctypes binding of libecq.so (the C ABI declared in include/ecq.h).
+
+The shared library is built in-tree by ``ecq_b200.build`` and loaded from
+``ecq_b200/_lib/libecq.so``. There is no fallback: if the library is missing
+or does not export the expected symbols, loading fails with an error.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_int32, c_int64, c_uint16, c_uint32, c_uint64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libecq.so"
+
+ECQ_OK = 0
+ERRORS = {
+    -1: "bad argument",
+    -2: "unsupported or inconsistent shape",
+    -3: "frequency table does not sum to 16384",
+    -4: "a symbol that occurs has frequency 0",
+    -5: "output buffer too small",
+    -6: "CUDA error",
+    -7: "internal error",
+    -8: "configuration not supported by the compiled kernels",
+    -9: "workspace missing or too small",
+}
+STATUS_CORRUPT = 1
+STATUS_TIMEOUT = 2
+STATUS_BADARG = 4
+FLAG_CONSTANT = 1
+TILE_ROWS = 8
+TABLE_ENTRIES = 16384
+
+# every symbol include/ecq.h declares
+EXPORTS = (
+    "ecq_version",
+    "ecq_table_from_counts",
+    "ecq_build_decode_table",
+    "ecq_encode_interleaved_host",
+    "ecq_matrix_encoded_bound",
+    "ecq_encode_matrix_host",
+    "ecq_decode_interleaved",
+    "ecq_matrix_decode",
+    "ecq_gemv_workspace_bytes",
+    "ecq_gemv",
+    "ecq_device_info",
+)
+
+
+class EcqError(RuntimeError):
+    pass
+
+
+class MatrixView(ctypes.Structure):
+    """Mirror of ``ecq_matrix_view``."""
+
+    _fields_ = [
+        ("rows", c_uint32), ("cols", c_uint32),
+        ("tile_rows", c_uint32), ("tile_cols", c_uint32),
+        ("group_size", c_uint32), ("n_tiles", c_uint32),
+        ("max_tile_bytes", c_uint32), ("flags", c_uint32),
+        ("data", c_void_p), ("tile_offset", c_void_p),
+        ("stream_len", c_void_p), ("dec_table", c_void_p),
+    ]
+
+
+_lib = None
+
+
+def _declare(L: ctypes.CDLL) -> None:
+    P = c_void_p
+    sig = {
+        "ecq_version": (c_int32, []),
+        "ecq_table_from_counts": (c_int32, [P, P, P]),
+        "ecq_build_decode_table": (c_int32, [P, P, P]),
+        "ecq_encode_interleaved_host": (c_int64, [P, c_int64, c_int32, P, P, c_int64, P, P]),
+        "ecq_matrix_encoded_bound": (c_int64, [c_uint32, c_uint32, c_uint32, c_uint32]),
+        "ecq_encode_matrix_host": (c_int32, [P, c_uint32, c_uint32, c_uint32, c_uint32, P, c_int32, P, c_int64, P, P, P]),
+        "ecq_decode_interleaved": (c_int32, [P, P, c_uint32, c_uint64, c_uint32, P, c_uint32, P, P, P]),
+        "ecq_matrix_decode": (c_int32, [POINTER(MatrixView), P, P, P]),
+        "ecq_gemv_workspace_bytes": (c_int64, [POINTER(MatrixView), c_uint32]),
+        "ecq_gemv": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, c_int64, P, P]),
+        "ecq_device_info": (c_int32, [P, P, P, POINTER(MatrixView)]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+
+
+def lib() -> ctypes.CDLL:
+    """Load libecq.so (building it first if it is absent and nvcc exists)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            from . import build as _build
+
+            _build.build()
+        if not LIB_PATH.exists():
+            raise EcqError(f"libecq.so not found at {LIB_PATH}; run python -m ecq_b200.build")
+        L = ctypes.CDLL(str(LIB_PATH))
+        missing = [s for s in EXPORTS if not hasattr(L, s)]
+        if missing:
+            raise EcqError(f"libecq.so lacks symbols: {missing}")
+        _declare(L)
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str) -> int:
+    if rc < 0:
+        raise EcqError(f"{what}: {ERRORS.get(int(rc), 'error')} ({rc})")
+    return rc
+
+
+def ptr(a) -> int:
+    """Raw address of a numpy array or torch tensor (None -> 0)."""
+    if a is None:
+        return 0
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    return a.ctypes.data
+
+
+__all__ = ["lib", "check", "ptr", "MatrixView", "EcqError", "EXPORTS", "c_uint16"]

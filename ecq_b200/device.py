@@ -1,0 +1,150 @@
+"""Device-resident packed matrices and the GPU entry points behind them.
+
+``DeviceMatrix`` holds one packed matrix in HBM (torch tensors own the
+memory): the tiles' interleaved stream bytes, tile offsets, per-stream
+lengths and the packed decode table, plus the fused GEMV's workspace and a
+device status word. Its methods call libecq's C ABI on the current torch
+stream; nothing here synchronises the host unless asked to.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import MatrixView, EcqError, check, lib, ptr
+from .codec import EncodedMatrix, RANSTable
+
+
+def _stream_ptr(stream=None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(s.cuda_stream)
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+@dataclass
+class DeviceMatrix:
+    rows: int
+    cols: int
+    tile_rows: int
+    tile_cols: int
+    group_size: int
+    table: RANSTable
+    flags: int
+    max_tile_bytes: int
+    data: torch.Tensor        # uint8
+    tile_offset: torch.Tensor  # int32 (bit pattern of uint32)
+    stream_len: torch.Tensor   # int16 (bit pattern of uint16)
+    dec_table: torch.Tensor    # int32 (bit pattern of uint32)
+    workspace: torch.Tensor    # uint8, zero-filled
+    status: torch.Tensor       # int32 [1]
+
+    @classmethod
+    def from_encoded(cls, enc: EncodedMatrix, group_size: int = 128, device="cuda") -> "DeviceMatrix":
+        entries, flags = enc.table.decode_table()
+        dev = torch.device(device)
+        data = np.ascontiguousarray(enc.data)
+        if data.size == 0:
+            data = np.zeros(16, dtype=np.uint8)
+        to = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a).view(dt)).to(dev)
+        m = cls(rows=enc.rows, cols=enc.cols, tile_rows=enc.tile_rows, tile_cols=enc.tile_cols,
+                group_size=int(group_size), table=enc.table, flags=flags, max_tile_bytes=enc.max_tile_bytes,
+                data=to(data, np.uint8), tile_offset=to(enc.tile_offset.astype(np.uint32), np.int32),
+                stream_len=to(enc.stream_len.astype(np.uint16), np.int16), dec_table=to(entries, np.int32),
+                workspace=torch.zeros(0, dtype=torch.uint8, device=dev),
+                status=torch.zeros(1, dtype=torch.int32, device=dev))
+        if int(enc.tile_offset[-1]) > enc.data.size:
+            raise ValueError("tile offsets run past the data")
+        ws = lib().ecq_gemv_workspace_bytes(ctypes_view(m), 1)
+        check(ws, "workspace size")
+        m.workspace = torch.zeros(int(ws), dtype=torch.uint8, device=dev)
+        return m
+
+    @property
+    def n_tiles(self) -> int:
+        return int(self.tile_offset.numel() - 1)
+
+    @property
+    def compressed_bytes(self) -> int:
+        return int(self.data.numel())
+
+    @property
+    def device(self) -> torch.device:
+        return self.data.device
+
+    def view(self) -> MatrixView:
+        return ctypes_view(self)
+
+    # ---- entry points ----
+    def decode(self, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Decode to row-major uint8 symbols [rows, cols] on the device."""
+        if out is None:
+            out = torch.empty(self.rows, self.cols, dtype=torch.uint8, device=self.device)
+        _require_cuda(out, "out")
+        if out.numel() != self.rows * self.cols or out.dtype != torch.uint8:
+            raise ValueError("out must be uint8 [rows, cols]")
+        v = self.view()
+        check(lib().ecq_matrix_decode(v, ptr(out), ptr(self.status), _stream_ptr(stream)), "matrix decode")
+        return out
+
+    def gemv(self, x: torch.Tensor, scales: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """y[b] = W_deq x[b] (fp16 in/out, fp32 accumulation); x [B, cols] or [cols]."""
+        squeeze = x.dim() == 1
+        x2 = x.reshape(-1, self.cols)
+        if x2.dtype != torch.float16:
+            raise ValueError("x must be float16")
+        _require_cuda(x2, "x")
+        _require_cuda(scales, "scales")
+        ng = (self.cols + self.group_size - 1) // self.group_size
+        if scales.dtype != torch.float16 or tuple(scales.shape) != (self.rows, ng):
+            raise ValueError(f"scales must be float16 [{self.rows}, {ng}]")
+        B = x2.shape[0]
+        if out is None:
+            out = torch.empty(B, self.rows, dtype=torch.float16, device=self.device)
+        _require_cuda(out, "out")
+        v = self.view()
+        check(lib().ecq_gemv(v, ptr(x2), ptr(scales), ptr(out), B, ptr(self.workspace), self.workspace.numel(),
+                             ptr(self.status), _stream_ptr(stream)), "gemv")
+        return out[0] if squeeze else out
+
+    def read_status(self, reset: bool = True) -> int:
+        """Synchronising read of the device status word (ECQ_STATUS_* bits)."""
+        s = int(self.status.item())
+        if reset and s:
+            self.status.zero_()
+            # a call that did not finish may leave slab counters set
+            self.workspace.zero_()
+        return s
+
+    def check(self) -> None:
+        s = self.read_status()
+        if s & _lib.STATUS_CORRUPT:
+            raise EcqError("corrupt rANS stream (end-of-stream state check failed)")
+        if s & _lib.STATUS_TIMEOUT:
+            raise EcqError("device wait timed out")
+        if s:
+            raise EcqError(f"device status {s:#x}")
+
+
+def ctypes_view(m: DeviceMatrix) -> MatrixView:
+    return MatrixView(rows=m.rows, cols=m.cols, tile_rows=m.tile_rows, tile_cols=m.tile_cols,
+                      group_size=m.group_size, n_tiles=m.n_tiles, max_tile_bytes=m.max_tile_bytes, flags=m.flags,
+                      data=ptr(m.data), tile_offset=ptr(m.tile_offset), stream_len=ptr(m.stream_len),
+                      dec_table=ptr(m.dec_table))
+
+
+def device_info(m: DeviceMatrix | None = None) -> dict:
+    sms = np.zeros(1, dtype=np.int32)
+    ctas = np.zeros(1, dtype=np.int32)
+    warps = np.zeros(1, dtype=np.int32)
+    v = ctypes_view(m) if m is not None else None
+    check(lib().ecq_device_info(ptr(sms), ptr(ctas), ptr(warps), v), "device_info")
+    return {"sm_count": int(sms[0]), "gemv_ctas": int(ctas[0]), "gemv_warps_per_cta": int(warps[0])}

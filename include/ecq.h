@@ -1,0 +1,177 @@
+/*
+ * ecq.h -- C ABI of libecq, the B200 (sm_100a) implementation of ecq's hot
+ * path: interleaved rANS decode of 4-bit weight symbols fused with per-group
+ * dequantisation and the GEMV that consumes them.
+ *
+ * Conventions
+ *   - Every function returns int32_t status (ECQ_OK == 0, negative on error)
+ *     unless it returns a size (int64_t, negative on error).
+ *   - Device pointers are owned by the caller; the library never frees caller
+ *     memory and launches allocate nothing. Every launch takes a cudaStream_t
+ *     (passed as void*, NULL = legacy default stream) and never synchronises
+ *     the host.
+ *   - Device-side failures are reported through a caller-provided uint32_t
+ *     status word in device memory (bits ECQ_STATUS_*), OR-ed in by kernels.
+ *   - Thread-safe: there is no global mutable state except the lazily read
+ *     device properties.
+ *
+ * Codec parameters are the reference's (drxddy/ecq src/rans.py:21-23): 16
+ * symbols, 14-bit probabilities, 32-bit state, L = 2^23, byte renormalisation.
+ * Stream format: src/interleaved_rans.py:76-153 (byte p of stream j at
+ * data[j + p*S], streams zero-padded to the longest).
+ */
+#ifndef ECQ_H
+#define ECQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ECQ_VERSION 100
+#define ECQ_NSYM 16
+#define ECQ_PROB_BITS 14
+#define ECQ_RANS_L (1u << 23)
+#define ECQ_LANES 32                  /* streams per tile in the packed format */
+#define ECQ_MAX_SYMS_PER_STREAM 1024  /* tile_rows*tile_cols/32 upper bound */
+#define ECQ_TABLE_ENTRIES 16384
+
+/* status codes */
+#define ECQ_OK 0
+#define ECQ_ERR_ARG (-1)
+#define ECQ_ERR_SHAPE (-2)
+#define ECQ_ERR_TABLE (-3)
+#define ECQ_ERR_ZERO_FREQ (-4)   /* a present symbol has frequency 0 */
+#define ECQ_ERR_CAPACITY (-5)
+#define ECQ_ERR_CUDA (-6)
+#define ECQ_ERR_INTERNAL (-7)
+#define ECQ_ERR_UNSUPPORTED (-8)
+#define ECQ_ERR_WORKSPACE (-9)
+
+/* device status word bits */
+#define ECQ_STATUS_CORRUPT 1u   /* a stream did not end in (state 2^23, all bytes read) */
+#define ECQ_STATUS_TIMEOUT 2u   /* a bounded wait on an mbarrier gave up */
+#define ECQ_STATUS_BADARG 4u
+
+/* normaliser used by ecq_table_from_counts */
+#define ECQ_NORMALISER_REFERENCE 0
+#define ECQ_NORMALISER_CLAMPED 1
+
+/* ecq_build_decode_table flags */
+#define ECQ_FLAG_CONSTANT 1u            /* one symbol has frequency 16384 */
+#define ECQ_FLAG_CONSTANT_SYM_SHIFT 4   /* its index, in bits 4..7 */
+
+/*
+ * Packed matrix: an [rows, cols] matrix of 4-bit symbols cut into tiles of
+ * tile_rows x tile_cols (cols % tile_cols == 0, tile_cols % 32 == 0; the last
+ * row slab may be short). Tiles are ordered row-slab major, then along K.
+ * Tile t's row-major symbols are ONE reference interleaved tile with 32
+ * streams, stored verbatim at data + tile_offset[t] (32*max_len bytes,
+ * always a multiple of 32); stream_len[32*t + j] is stream j's byte length.
+ * dec_table is the 16384-entry packed decode table from
+ * ecq_build_decode_table for the matrix's frequency table.
+ */
+typedef struct ecq_matrix_view {
+    uint32_t rows, cols;
+    uint32_t tile_rows, tile_cols;
+    uint32_t group_size;       /* scales are [rows, ceil(cols/group_size)] */
+    uint32_t n_tiles;          /* ceil(rows/tile_rows) * cols/tile_cols */
+    uint32_t max_tile_bytes;   /* max over tiles of 32*max_len */
+    uint32_t flags;            /* from ecq_build_decode_table */
+    const uint8_t *data;       /* device */
+    const uint32_t *tile_offset; /* device, n_tiles + 1 entries */
+    const uint16_t *stream_len;  /* device, 32 * n_tiles entries */
+    const uint32_t *dec_table;   /* device, 16384 entries */
+} ecq_matrix_view;
+
+int32_t ecq_version(void);
+
+/* ---------------- host-side codec ---------------- */
+
+/* Frequency table from a 16-bin histogram. Replaces RANSTable.from_counts
+ * (src/rans.py:39-60) and gives the same table, except where that normaliser
+ * gives frequency 0 to a symbol that occurs (its encoder never terminates on
+ * such input): then every frequency is raised to at least 1 before the
+ * remainder goes to the largest, and *normaliser = ECQ_NORMALISER_CLAMPED. */
+int32_t ecq_table_from_counts(const uint64_t *counts, uint32_t *freq, int32_t *normaliser);
+
+/* 16384 packed decode entries {sym:4 | freq:14 | slot-cumfreq:14} for a
+ * frequency table summing to 16384. Replaces the sym_table/freq/cumfreq
+ * triple the reference's kernels read (src/rans.py:51-58,
+ * src/metal_interleaved.py:52-117). */
+int32_t ecq_build_decode_table(const uint32_t *freq, uint32_t *entries, uint32_t *flags);
+
+/* Interleaved encoder, byte-identical to interleaved_rans_encode
+ * (src/interleaved_rans.py:76-153). Writes n_streams*max_len bytes into
+ * data; returns that byte count or a negative error. */
+int64_t ecq_encode_interleaved_host(const uint8_t *symbols, int64_t n, int32_t n_streams,
+                                    const uint32_t *freq, uint8_t *data, int64_t data_cap,
+                                    uint32_t *stream_lengths, uint32_t *max_len);
+
+/* Worst-case byte size of ecq_encode_matrix_host's data output. */
+int64_t ecq_matrix_encoded_bound(uint32_t rows, uint32_t cols, uint32_t tile_rows, uint32_t tile_cols);
+
+/* Encode a row-major [rows, cols] symbol matrix into the packed format over
+ * n_threads host threads (<= 0: all). Each tile is one call of the
+ * reference's interleaved_rans_encode with 32 streams
+ * (src/interleaved_rans.py:76-153); replaces the per-layer encode loop of
+ * experiments/e2e_validation.py:49-105. tile_offset gets n_tiles+1 entries. */
+int32_t ecq_encode_matrix_host(const uint8_t *symbols, uint32_t rows, uint32_t cols, uint32_t tile_rows,
+                               uint32_t tile_cols, const uint32_t *freq, int32_t n_threads, uint8_t *data,
+                               int64_t data_cap, uint32_t *tile_offset, uint16_t *stream_len,
+                               int64_t *total_bytes);
+
+/* ---------------- device: decode ---------------- */
+
+/* Decode one reference tile (any n_streams >= 1, any n_symbols) on the GPU:
+ * d_data holds the tile's interleaved bytes (n_streams*max_len), d_lengths
+ * its stream lengths, d_dec_table the packed table. Output d_out[n_symbols].
+ * Replaces interleaved_rans_decode (src/interleaved_rans.py:156-217) and
+ * MetalInterleavedRANS.decode (src/metal_interleaved.py:833-885, kernel
+ * parallel_rans_decode :52-117). Semantics are the reference's, guards
+ * included: streams shorter than 4 bytes decode to zeros and
+ * renormalisation stops at the stream length, so damaged tiles decode to
+ * the same bytes the reference returns. Streams that do not end in
+ * (state 2^23, all bytes read) set ECQ_STATUS_CORRUPT in *d_status. */
+int32_t ecq_decode_interleaved(const uint8_t *d_data, const uint32_t *d_lengths, uint32_t n_streams,
+                               uint64_t n_symbols, uint32_t max_len, const uint32_t *d_dec_table,
+                               uint32_t decode_flags, uint8_t *d_out, uint32_t *d_status, void *stream);
+
+/* Decode a packed matrix to row-major uint8 symbols d_out[rows*cols] (the
+ * CACHED strategy: DecodeOnceStrategy.load_layer,
+ * src/decode_strategies.py:43-73, and the GPU_ASYNC decode kernel
+ * parallel_rans_decode_async, src/decode_strategies.py:336-390). */
+int32_t ecq_matrix_decode(const ecq_matrix_view *m, uint8_t *d_out, uint32_t *d_status, void *stream);
+
+/* ---------------- device: fused decode + dequant + GEMV ---------------- */
+
+/* Bytes of device workspace ecq_gemv needs for this matrix and batch. The
+ * workspace must be zero-filled once before first use; ecq_gemv leaves it
+ * zeroed again on completion, so it can be reused across calls on one
+ * stream (calls that overlap on the GPU must use distinct workspaces). */
+int64_t ecq_gemv_workspace_bytes(const ecq_matrix_view *m, uint32_t batch);
+
+/* y[b, r] = sum_c (sym[r,c] - 8) * scales[r, c/g] * x[b, c], fp32
+ * accumulation, fp16 output, for b < batch. x is [batch, cols] fp16,
+ * scales [rows, ceil(cols/g)] fp16, y [batch, rows] fp16 (all device,
+ * row-major, contiguous). The dequantisation is the reference's
+ * sym*scale + zero with zero = -8*scale (src/quantizer.py:33-35). Replaces
+ * the fused kernels fused_parallel_gemv / fused_parallel_gemv_cached /
+ * tiled_parallel_gemm (src/metal_interleaved.py:130-484) and the MLX-side
+ * entropy_coded_matmul (docs/mlx_integration_plan.md:222-237). No decoded
+ * weight is written to memory. */
+int32_t ecq_gemv(const ecq_matrix_view *m, const void *x_f16, const void *scales_f16, void *y_f16,
+                 uint32_t batch, void *workspace, int64_t workspace_bytes, uint32_t *d_status, void *stream);
+
+/* Number of SMs and the persistent grid the fused kernel uses (for tests
+ * and the benchmark's launch accounting). */
+int32_t ecq_device_info(int32_t *sm_count, int32_t *gemv_ctas, int32_t *gemv_warps_per_cta,
+                        const ecq_matrix_view *m);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ECQ_H */

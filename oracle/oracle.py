@@ -61,6 +61,9 @@ def lib() -> ctypes.CDLL:
         L.oracle_decode_interleaved.restype = ctypes.c_int
         L.oracle_dequant_gemv.argtypes = [P, ctypes.c_long, ctypes.c_long, P, ctypes.c_long, P, P]
         L.oracle_dequant_gemv.restype = None
+        L.oracle_gemv_packed.argtypes = [P, P, P, ctypes.c_long, ctypes.c_long, ctypes.c_long, ctypes.c_long,
+                                         P, P, ctypes.c_long, P, ctypes.c_long, ctypes.c_long, P]
+        L.oracle_gemv_packed.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -180,6 +183,44 @@ def encode_matrix_tiles(symbols, freq, tile_rows: int, tile_cols: int, n_streams
     for r0, nr, c0, nc in tile_grid(M, K, tile_rows, tile_cols):
         out.append(encode_interleaved(sym[r0:r0 + nr, c0:c0 + nc].reshape(-1), freq, n_streams))
     return out
+
+
+def gemv_packed(data, tile_offset, stream_len, rows, cols, tile_rows, tile_cols, freq, scales, group_size, x,
+                threads: int = 1, tile_range=None):
+    """The reference CPU path (decode each tile, dequantise, matvec) over a
+    packed matrix, using `threads` host threads over disjoint row slabs
+    (ctypes releases the GIL). Returns (y float32 [rows], bad_streams)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    d = np.ascontiguousarray(data, dtype=np.uint8)
+    off = np.ascontiguousarray(tile_offset, dtype=np.uint32)
+    lens = np.ascontiguousarray(stream_len, dtype=np.uint16)
+    f = np.ascontiguousarray(freq, dtype=np.uint32)
+    sc = np.ascontiguousarray(scales, dtype=np.float32)
+    xv = np.ascontiguousarray(np.asarray(x, dtype=np.float32).reshape(-1))
+    y = np.zeros(rows, dtype=np.float64)
+    nk = cols // tile_cols
+    n_tiles = off.size - 1
+    lo, hi = (0, n_tiles) if tile_range is None else tile_range
+    slab_lo, slab_hi = lo // nk, (hi + nk - 1) // nk
+    threads = max(1, int(threads))
+    bounds = np.linspace(slab_lo, slab_hi, threads + 1).astype(np.int64)
+    L = lib()
+
+    def run(i):
+        t0 = max(lo, int(bounds[i]) * nk)
+        t1 = min(hi, int(bounds[i + 1]) * nk)
+        if t1 <= t0:
+            return 0
+        return L.oracle_gemv_packed(_p(d), _p(off), _p(lens), rows, cols, tile_rows, tile_cols, _p(f), _p(sc),
+                                    int(group_size), _p(xv), t0, t1, _p(y))
+
+    if threads == 1:
+        bad = run(0)
+    else:
+        with ThreadPoolExecutor(threads) as ex:
+            bad = sum(ex.map(run, range(threads)))
+    return y.astype(np.float32), int(bad)
 
 
 def cpu_count() -> int:

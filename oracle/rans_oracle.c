@@ -207,3 +207,37 @@ void oracle_dequant_gemv(const uint8_t *sym, long M, long K, const float *scale,
         y[r] = (float)acc;
     }
 }
+
+/* The reference's CPU path over the tiles [t0, t1) of a packed matrix:
+ * interleaved_rans_decode per tile (src/interleaved_rans.py:156-217), then
+ * dequantise (sym - 8) * scale (src/quantizer.py:33-35) and accumulate the
+ * matvec into y_acc (double, indexed by row). Tiles are 32-stream tiles of
+ * tile_rows x tile_cols, row-slab major. Callers that run several ranges
+ * in parallel give each a disjoint set of row slabs. Returns the number of
+ * streams that failed the end-state check. */
+int oracle_gemv_packed(const uint8_t *data, const uint32_t *tile_offset, const uint16_t *stream_len,
+                       long rows, long cols, long tile_rows, long tile_cols, const uint32_t *freq,
+                       const float *scales, long g, const float *x, long t0, long t1, double *y_acc) {
+    long nk = cols / tile_cols;
+    long ng = (cols + g - 1) / g;
+    uint8_t *sym = (uint8_t *)malloc((size_t)(tile_rows * tile_cols));
+    uint32_t lens[32];
+    int bad = 0;
+    for (long t = t0; t < t1; t++) {
+        long slab = t / nk, k = t % nk;
+        long r0 = slab * tile_rows, c0 = k * tile_cols;
+        long nr = rows - r0 < tile_rows ? rows - r0 : tile_rows;
+        for (int j = 0; j < 32; j++) lens[j] = stream_len[t * 32 + j];
+        bad += oracle_decode_interleaved(data + tile_offset[t], lens, 32, nr * tile_cols, freq, sym, NULL, NULL);
+        for (long r = 0; r < nr; r++) {
+            double acc = 0.0;
+            const uint8_t *sr = sym + r * tile_cols;
+            const float *sc = scales + (r0 + r) * ng;
+            for (long c = 0; c < tile_cols; c++)
+                acc += ((double)sr[c] - 8.0) * (double)sc[(c0 + c) / g] * (double)x[c0 + c];
+            y_acc[r0 + r] += acc;
+        }
+    }
+    free(sym);
+    return bad;
+}

@@ -1,0 +1,30 @@
+"""The C-ABI library loads and exports every function include/ecq.h declares
+(no device calls)."""
+import re
+from pathlib import Path
+
+from ecq_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "ecq.h"
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:int32_t|int64_t|void)\s+(ecq_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_and_binding_agree():
+    assert declared_functions() == sorted(_lib.EXPORTS)
+
+
+def test_library_exports_all_symbols():
+    L = _lib.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+    assert L.ecq_version() == 100
+
+
+def test_workspace_size_query_is_host_only():
+    v = _lib.MatrixView(rows=4096, cols=4096, tile_rows=8, tile_cols=512, group_size=128, n_tiles=4096)
+    assert _lib.lib().ecq_gemv_workspace_bytes(v, 1) == 4096 * 8 * 4 + 512 * 4

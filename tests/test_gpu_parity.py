@@ -1,0 +1,172 @@
+"""GPU parity: libecq's kernels against the oracle and the reference golden
+vectors. Symbols must be bit-exact; GEMV outputs within max relative error
+2e-3 of the float64 oracle (fp16 output). All calls go through the C ABI."""
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, load_cases
+from oracle import oracle
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import ecq_b200 as ecq  # noqa: E402
+from ecq_b200 import synthetic as syn  # noqa: E402
+
+RTOL = 2e-3  # max|y - y_ref| / max|y_ref|, the path's stated tolerance
+
+
+def _rel_err(y, y_ref):
+    y = np.asarray(y, dtype=np.float64)
+    y_ref = np.asarray(y_ref, dtype=np.float64)
+    return float(np.max(np.abs(y - y_ref)) / max(np.max(np.abs(y_ref)), 1e-30))
+
+
+@pytest.fixture(scope="module", autouse=True)
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.init()
+
+
+def test_decode_reference_tiles_bit_exact():
+    cases, _ = load_cases(GOLDEN / "codec.npz")
+    dec = ecq.CudaInterleavedRANS()
+    for c in cases:
+        tile = ecq.InterleavedEncodedTile(data=bytes(c["data"]), stream_lengths=c["lengths"].tolist(),
+                                          max_stream_len=int(c["max_len"]), n_symbols=int(c["symbols"].size),
+                                          n_streams=int(c["S"]), table=ecq.RANSTable.from_freq(c["freq"]))
+        out = dec.decode(tile)
+        assert np.array_equal(out, c["symbols"]), str(c["name"])
+        assert dec.last_status == 0, str(c["name"])
+
+
+def test_decode_corrupt_tiles_like_reference():
+    cases, z = load_cases(GOLDEN / "corrupt.npz", prefix="k")
+    dec = ecq.CudaInterleavedRANS()
+    for c in cases:
+        tile = ecq.InterleavedEncodedTile(data=bytes(c["data"]), stream_lengths=c["lengths"].tolist(),
+                                          max_stream_len=int(z["max_len"]), n_symbols=int(z["n_symbols"]),
+                                          n_streams=32, table=ecq.RANSTable.from_freq(z["freq"]))
+        out = dec.decode(tile)
+        assert np.array_equal(out, c["out"]), str(c["name"])
+        assert (dec.last_status == 0) == (str(c["name"]) == "intact")
+
+
+def test_c1_single_matrix():
+    z = np.load(GOLDEN / "c1.npz")
+    tile = ecq.InterleavedEncodedTile(data=bytes(z["data"]), stream_lengths=z["lengths"].tolist(),
+                                      max_stream_len=int(z["max_len"]), n_symbols=int(z["symbols"].size),
+                                      n_streams=int(z["S"]), table=ecq.RANSTable.from_freq(z["freq"]))
+    out = ecq.interleaved_rans_decode(tile)
+    assert np.array_equal(out.reshape(z["symbols"].shape), z["symbols"])
+    # the same matrix through the packed format and the fused GEMV
+    enc = ecq.encode_matrix(z["symbols"], ecq.RANSTable.from_freq(z["freq"]), group_size=128)
+    m = ecq.DeviceMatrix.from_encoded(enc, group_size=128)
+    y = m.gemv(torch.from_numpy(z["x"]).cuda(), torch.from_numpy(z["scales"]).cuda())
+    m.check()
+    assert _rel_err(y.float().cpu().numpy(), z["y"]) <= RTOL
+
+
+CASES = [
+    # rows, cols, tile_cols, group, b
+    (64, 512, 512, 128, 0.5),
+    (36, 768, 256, 128, 0.5),
+    (17, 384, 128, 64, 2.0),
+    (128, 1024, 512, 32, 0.3),
+    (40, 1024, 256, 256, 1.0),
+    (96, 2048, 512, 512, 100.0),
+    (8, 128, 128, 128, 0.5),
+    (1, 512, 512, 128, 0.5),
+    (300, 1536, 512, 64, 0.5),
+]
+
+
+@pytest.mark.parametrize("rows,cols,tc,g,b", CASES)
+def test_packed_decode_and_gemv(rows, cols, tc, g, b):
+    sym = syn.laplace_symbols(rows, cols, b=b, seed=rows + cols)
+    sc = syn.group_scales(rows, cols, g, seed=1)
+    x = syn.activations(1, cols, seed=2)
+    enc = ecq.encode_matrix(sym, tile_cols=tc, group_size=g)
+    m = ecq.DeviceMatrix.from_encoded(enc, group_size=g)
+    out = m.decode()
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), sym)
+    y = m.gemv(torch.from_numpy(x).cuda(), torch.from_numpy(sc).cuda())
+    m.check()
+    y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), g, x.astype(np.float32))
+    assert _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL
+
+
+def test_gemv_deterministic_and_workspace_reusable():
+    sym = syn.laplace_symbols(512, 4096, b=0.5, seed=3)
+    sc = torch.from_numpy(syn.group_scales(512, 4096, 128)).cuda()
+    x = torch.from_numpy(syn.activations(1, 4096)).cuda()
+    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, group_size=128), group_size=128)
+    ys = [m.gemv(x, sc).clone() for _ in range(3)]
+    m.check()
+    for y in ys[1:]:
+        assert torch.equal(y, ys[0])
+    assert int(m.workspace[-(512 // 8) * 4:].count_nonzero()) == 0  # slab counters back at zero
+
+
+def test_constant_matrix():
+    sym = np.full((24, 512), 11, dtype=np.uint8)
+    t = ecq.RANSTable.from_symbols(sym)  # reference normaliser gives 16384 to the one symbol
+    assert t.freq.max() == 16384
+    sc = syn.group_scales(24, 512, 128)
+    x = syn.activations(1, 512)
+    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, t, group_size=128), group_size=128)
+    assert np.array_equal(m.decode().cpu().numpy(), sym)
+    y = m.gemv(torch.from_numpy(x).cuda(), torch.from_numpy(sc).cuda())
+    m.check()
+    y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), 128, x.astype(np.float32))
+    assert _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL
+
+
+def test_student_t_quantised_weights():
+    w = syn.student_t_weights(256, 1024, seed=3)
+    sym, sc = syn.quantize_symmetric_groups(w, 128)
+    x = syn.activations(1, 1024)
+    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, group_size=128), group_size=128)
+    y = m.gemv(torch.from_numpy(x).cuda(), torch.from_numpy(sc).cuda())
+    m.check()
+    y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), 128, x.astype(np.float32))
+    assert _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL
+
+
+def test_corrupt_packed_tile_sets_status():
+    sym = syn.laplace_symbols(64, 512, b=0.5, seed=9)
+    enc = ecq.encode_matrix(sym, group_size=128)
+    enc.data[enc.tile_offset[3] + 40] ^= 0xFF  # damage one byte of tile 3
+    m = ecq.DeviceMatrix.from_encoded(enc, group_size=128)
+    m.decode()
+    assert m.read_status() & 1
+
+
+def test_batched_gemv():
+    sym = syn.laplace_symbols(96, 1024, b=0.5, seed=4)
+    sc = syn.group_scales(96, 1024, 128)
+    x = syn.activations(4, 1024)
+    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, group_size=128), group_size=128)
+    y = m.gemv(torch.from_numpy(x).cuda(), torch.from_numpy(sc).cuda())
+    m.check()
+    y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), 128, x.astype(np.float32))
+    assert _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL
+
+
+@pytest.mark.parametrize("M,K", [(4096, 4096), (11008, 4096), (4096, 11008)])
+def test_llama_shapes_full_size(M, K):
+    """Full-size layer shapes: decode(encode(W)) == W and the fused GEMV
+    against the float64 oracle."""
+    sym = syn.laplace_symbols(M, K, b=0.5, seed=0)
+    sc = syn.group_scales(M, K, 128, seed=1)
+    x = syn.activations(1, K, seed=2)
+    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, group_size=128), group_size=128)
+    out = m.decode()
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), sym)
+    y = m.gemv(torch.from_numpy(x).cuda(), torch.from_numpy(sc).cuda())
+    m.check()
+    y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), 128, x.astype(np.float32))
+    assert _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL
