@@ -79,7 +79,7 @@ class RANSTable:
         return cls.from_counts(f)
 
     def decode_table(self) -> tuple[np.ndarray, int]:
-        """16384 packed device entries {sym:4 | freq:14 | slot-cumfreq:14}
+        """16384 packed device entries (slot - cumfreq) | sym << 14 | freq << 18
         and the flags word (ECQ_FLAG_CONSTANT for a single-symbol table)."""
         e = np.zeros(PROB_SCALE, dtype=np.uint32)
         fl = np.zeros(1, dtype=np.uint32)

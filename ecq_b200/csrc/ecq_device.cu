@@ -87,6 +87,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         if (global_timer_ns() - t0 > kWaitLimitNs) return false;
     }
 }
+// 32-bit shared-window loads. Stream-byte loads stay ordered after the
+// mbarrier waits (volatile); table loads only depend on the decoded state.
+__device__ __forceinline__ uint32_t lds_u8(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -124,8 +136,8 @@ __global__ void __launch_bounds__(256) decode_interleaved_exact(const uint8_t* _
             sym = csym;  // freq 16384, cumfreq 0: the state is unchanged
         } else {
             const uint32_t e = table[x & 16383u];
-            sym = e & 15u;
-            x = ((e >> 4) & 16383u) * (x >> 14) + (e >> 18);
+            sym = (e >> 14) & 15u;
+            x = (e >> 18) * (x >> 14) + (e & 16383u);
         }
         out[j + i * S] = static_cast<uint8_t>(sym);
         while (x < kL && ptr < len) {
@@ -158,27 +170,73 @@ struct MatrixParams {
 };
 
 constexpr int kTileRows = 8;
+// {-(2^23 + 8*2^14), -(2^23 + 8*2^14)} as f32x2
+constexpr uint64_t kNegBias2 = 0xCB020000CB020000ull;
 
-// One decode step on lane state (x, a); a is the shared-memory address of
-// the lane's next stream byte (byte p of lane j at tile_base + 32p + j).
-__device__ __forceinline__ uint32_t decode_step(uint32_t& x, uint32_t& a, const uint32_t* __restrict__ table,
-                                                const uint8_t* __restrict__ smem_base) {
-    const uint32_t e = table[x & 16383u];
-    x = (e >> 18) + ((e >> 4) & 16383u) * (x >> 14);
-    if (x < kL) {
-        x = (x << 8) | smem_base[a];
-        a += 32;
-        if (x < kL) {
-            x = (x << 8) | smem_base[a];
-            a += 32;
-        }
-    }
-    return e & 15u;
+// (sym - 8) * 2^14 as an exact float, from a packed entry: the entry's sym
+// field (bits 14..17) ORed into the mantissa of 2^23 gives 2^23 + sym*2^14.
+constexpr float kWeightBias = 8519680.0f;  // 2^23 + 8 * 2^14
+__device__ __forceinline__ uint32_t entry_weight_bits(uint32_t e) { return (e & 0x3C000u) | 0x4B000000u; }
+__device__ __forceinline__ float entry_weight(uint32_t e) { return __int_as_float(entry_weight_bits(e)) - kWeightBias; }
+
+// packed f32x2 arithmetic (sm_100): two fp32 lanes in one 64-bit register pair
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+    return d;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+    uint32_t a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(a), "=r"(b) : "l"(v));
+    lo = __uint_as_float(a);
+    hi = __uint_as_float(b);
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
 }
 
-__device__ __forceinline__ float sym_minus8(uint32_t sym) {
-    // exact float(sym - 8) for sym < 16: (2^23 + sym) - (2^23 + 8)
-    return __int_as_float(0x4B000000u | sym) - 8388616.0f;
+// One decode step for this lane. tb is the shared-window address of the
+// packed decode table, a that of the lane's next stream byte (byte p of lane
+// j of a tile at tile_base + 32p + j). Returns the table entry.
+//
+// Renormalisation reads the next two bytes ahead of need and shifts in 0, 1
+// or 2 of them with one funnel shift. After a decode step of an intact
+// stream 2^9 <= x < 2^31, and the reference's byte loop reads one byte iff
+// x < 2^23 and a second iff x < 2^15. (A damaged stream may need a third,
+// which is not read; the end-of-stream check flags it.)
+__device__ __forceinline__ uint32_t decode_step(uint32_t& x, uint32_t& a, uint32_t tb) {
+    uint32_t e;
+    asm volatile(
+        "{\n\t"
+        ".reg .u32 b0, b1, sl, q, f, bi, nx, sh;\n\t"
+        ".reg .pred p1, p2;\n\t"
+        "ld.shared.u8 b0, [%1];\n\t"          // next two stream bytes, read ahead of need
+        "ld.shared.u8 b1, [%1+32];\n\t"
+        "and.b32 sl, %0, 16383;\n\t"          // slot
+        "mad.lo.u32 sl, sl, 4, %3;\n\t"
+        "ld.shared.u32 %2, [sl];\n\t"         // e = table[slot]
+        "shr.u32 q, %0, 14;\n\t"
+        "shr.u32 f, %2, 18;\n\t"
+        "and.b32 bi, %2, 16383;\n\t"
+        "mad.lo.u32 %0, f, q, bi;\n\t"        // x = freq * (x >> 14) + slot - cumfreq
+        "prmt.b32 nx, b1, b0, 0x4011;\n\t"    // b0 << 24 | b1 << 16
+        "setp.lt.u32 p1, %0, 8388608;\n\t"    // x < 2^23: one byte due
+        "setp.lt.u32 p2, %0, 32768;\n\t"      // x < 2^15: two bytes due
+        "selp.u32 sh, 8, 0, p1;\n\t"
+        "selp.u32 sh, 16, sh, p2;\n\t"
+        "shf.l.wrap.b32 %0, nx, %0, sh;\n\t"  // x = (x << sh) | (nx >> (32 - sh))
+        "mad.lo.u32 %1, sh, 4, %1;\n\t"       // 32 bytes per consumed byte
+        "}"
+        : "+r"(x), "+r"(a), "=r"(e)
+        : "r"(tb));
+    return e;
 }
 
 // Reduce v[0..7] over the 32 lanes; lane l ends with the total of row
@@ -211,72 +269,126 @@ __device__ __forceinline__ int reduce_row_of_lane(int lane) {
     return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
 }
 
+// Lane l < NSG holds the scale of scale-group l of this tile row (the NSG
+// groups a tile row spans); the others hold 0.
+template <int NSG, int GPL>
+__device__ __forceinline__ float load_row_scale(const MatrixParams& p, uint32_t row, uint32_t c0, int lane) {
+    if (lane >= NSG) return 0.f;
+    return __half2float(p.scales[static_cast<size_t>(row) * p.ng + (c0 + lane * GPL * 32) / p.group_size]);
+}
+
+// Finish one tile of the GEMV: reduce the lane partials over the warp,
+// publish the tile's 8 row sums, and let the last tile of a row slab sum the
+// slab's partials (fixed order, so y is deterministic) and write y.
+__device__ __forceinline__ void finish_tile(const MatrixParams& p, uint32_t t, float (&acc)[8], int rows_here,
+                                            int lane) {
+    // short slab: move row 0 to acc[0]
+#pragma unroll 1
+    for (int r = rows_here; r < kTileRows; ++r) {
+#pragma unroll
+        for (int k = 0; k < kTileRows - 1; ++k) acc[k] = acc[k + 1];
+        acc[kTileRows - 1] = 0.f;
+    }
+    const uint32_t slab = t / p.n_ktiles;
+    const uint32_t r0 = slab * kTileRows;
+    const float v = transpose_reduce8(acc, lane);
+    if ((lane & 3) == 0) p.partials[static_cast<size_t>(t) * kTileRows + reduce_row_of_lane(lane)] = v;
+    __threadfence();
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atomicAdd(p.slab_count + slab, 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == p.n_ktiles - 1) {
+        __threadfence();
+        const int row = lane & 7, kp = lane >> 3;
+        const float* base = p.partials + static_cast<size_t>(slab) * p.n_ktiles * kTileRows;
+        float s = 0.f;
+        for (uint32_t k = kp; k < p.n_ktiles; k += 4) s += __ldcg(base + static_cast<size_t>(k) * kTileRows + row);
+        s += __shfl_xor_sync(0xffffffffu, s, 8);
+        s += __shfl_xor_sync(0xffffffffu, s, 16);
+        if (kp == 0 && row < rows_here) p.y[r0 + row] = __float2half_rn(s);
+        if (lane == 0) p.slab_count[slab] = 0u;
+    }
+}
+
+// Decode one tile (buf = offset of its bytes in shared memory) and either
+// accumulate its GEMV contribution or store its symbols.
 template <int MPL, int GPL, bool GEMV, bool CONSTANT>
-__device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, uint32_t buf, const uint32_t* table,
-                                             const uint8_t* smem_base, int lane) {
-    constexpr int NSG = MPL / GPL;                      // group segments per tile row
-    constexpr int NSC = (kTileRows * NSG + 31) / 32;    // scales held per lane
+__device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, uint32_t buf, uint32_t tb,
+                                             int lane) {
+    constexpr int NSG = MPL / GPL;  // scale groups per tile row
     const uint32_t slab = t / p.n_ktiles;
     const uint32_t kt = t - slab * p.n_ktiles;
     const uint32_t r0 = slab * kTileRows;
-    const uint32_t rows_here = min(static_cast<uint32_t>(kTileRows), p.rows - r0);
+    const int rows_here = static_cast<int>(min(static_cast<uint32_t>(kTileRows), p.rows - r0));
     const uint32_t c0 = kt * (MPL * 32);
     const uint32_t len = p.stream_len[t * 32 + lane];
 
-    uint32_t a = buf + lane;
-    uint32_t x = (static_cast<uint32_t>(smem_base[a]) << 24) | (static_cast<uint32_t>(smem_base[a + 32]) << 16) |
-                 (static_cast<uint32_t>(smem_base[a + 64]) << 8) | static_cast<uint32_t>(smem_base[a + 96]);
+    uint32_t a = buf + lane;  // shared-window address
+    uint32_t x = (lds_u8(a) << 24) | (lds_u8(a + 32) << 16) | (lds_u8(a + 64) << 8) | lds_u8(a + 96);
     a += 128;
-    const uint32_t csym = (p.flags >> ECQ_FLAG_CONSTANT_SYM_SHIFT) & 15u;
+    const uint32_t cent = ((p.flags >> ECQ_FLAG_CONSTANT_SYM_SHIFT) & 15u) << 14;  // constant table: sym field
 
-    float xr[MPL];
-    float sc[NSC];
+    float xs[MPL];  // x * 2^-14 (exact), this lane's columns of the tile
     float acc[kTileRows];
+    float sc = 0.f;
     if constexpr (GEMV) {
 #pragma unroll
-        for (int m = 0; m < MPL; ++m) xr[m] = __half2float(p.x[c0 + 32 * m + lane]);
-#pragma unroll
-        for (int i = 0; i < NSC; ++i) {
-            const int idx = lane + 32 * i;
-            const int r = idx / NSG, sg = idx - (idx / NSG) * NSG;
-            float s = 0.f;
-            if (r < static_cast<int>(rows_here))
-                s = __half2float(p.scales[static_cast<size_t>(r0 + r) * p.ng + (c0 + sg * GPL * 32) / p.group_size]);
-            sc[i] = s;
-        }
+        for (int m = 0; m < MPL; ++m) xs[m] = __half2float(p.x[c0 + 32 * m + lane]) * 6.103515625e-05f;
 #pragma unroll
         for (int r = 0; r < kTileRows; ++r) acc[r] = 0.f;
+        sc = load_row_scale<NSG, GPL>(p, r0, c0, lane);
     }
 
+#pragma unroll 1
+    for (int r = 0; r < rows_here; ++r) {
+        float rowacc = 0.f;
+        float sn = 0.f;
+        if constexpr (GEMV) {
+            if (r + 1 < rows_here) sn = load_row_scale<NSG, GPL>(p, r0 + r + 1, c0, lane);
+        }
 #pragma unroll
-    for (int r = 0; r < kTileRows; ++r) {
-        if (r < static_cast<int>(rows_here)) {
+        for (int sg = 0; sg < NSG; ++sg) {
+            float part = 0.f;
+            if constexpr (GEMV && !CONSTANT && (GPL % 2 == 0)) {
+                // two symbols per packed f32x2 add + fma
+                uint64_t part2 = 0;
 #pragma unroll
-            for (int sg = 0; sg < NSG; ++sg) {
-                float part = 0.f;
+                for (int mm = 0; mm < GPL; mm += 2) {
+                    const int m = sg * GPL + mm;
+                    const uint32_t e0 = decode_step(x, a, tb);
+                    const uint32_t e1 = decode_step(x, a, tb);
+                    const uint64_t w2 = add2(pack2(entry_weight_bits(e0), entry_weight_bits(e1)), kNegBias2);
+                    part2 = fma2(w2, pack2(__float_as_uint(xs[m]), __float_as_uint(xs[m + 1])), part2);
+                }
+                float lo, hi;
+                unpack2(part2, lo, hi);
+                part = lo + hi;
+            } else {
 #pragma unroll
                 for (int mm = 0; mm < GPL; ++mm) {
                     const int m = sg * GPL + mm;
-                    uint32_t sym;
+                    uint32_t e;
                     if constexpr (CONSTANT) {
-                        sym = csym;
+                        e = cent;
                     } else {
-                        sym = decode_step(x, a, table, smem_base);
+                        e = decode_step(x, a, tb);
                     }
                     if constexpr (GEMV) {
-                        part = fmaf(sym_minus8(sym), xr[m], part);
+                        part = fmaf(entry_weight(e), xs[m], part);
                     } else {
-                        p.sym_out[static_cast<size_t>(r0 + r) * p.cols + c0 + 32 * m + lane] = static_cast<uint8_t>(sym);
+                        p.sym_out[static_cast<size_t>(r0 + r) * p.cols + c0 + 32 * m + lane] =
+                            static_cast<uint8_t>((e >> 14) & 15u);
                     }
                 }
-                if constexpr (GEMV) {
-                    constexpr int idx0 = 0;
-                    (void)idx0;
-                    const int idx = r * NSG + sg;  // compile-time after unrolling
-                    const float s = __shfl_sync(0xffffffffu, sc[idx >> 5], idx & 31);
-                    acc[r] = fmaf(s, part, acc[r]);
-                }
             }
+            if constexpr (GEMV) rowacc = fmaf(__shfl_sync(0xffffffffu, sc, sg), part, rowacc);
+        }
+        if constexpr (GEMV) {
+#pragma unroll
+            for (int k = 0; k < kTileRows - 1; ++k) acc[k] = acc[k + 1];
+            acc[kTileRows - 1] = rowacc;
+            sc = sn;
         }
     }
     if constexpr (!CONSTANT) {
@@ -285,27 +397,15 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
         if (len != 4u) atomicOr(p.status, ECQ_STATUS_CORRUPT);
     }
 
-    if constexpr (GEMV) {
-        const float v = transpose_reduce8(acc, lane);
-        if ((lane & 3) == 0) p.partials[static_cast<size_t>(t) * kTileRows + reduce_row_of_lane(lane)] = v;
-        __threadfence();
-        __syncwarp();
-        uint32_t old = 0;
-        if (lane == 0) old = atomicAdd(p.slab_count + slab, 1u);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        if (old == p.n_ktiles - 1) {
-            // last tile of this row slab: sum the slab's partials in fixed order
-            __threadfence();
-            const int row = lane & 7, kp = lane >> 3;
-            const float* base = p.partials + static_cast<size_t>(slab) * p.n_ktiles * kTileRows;
-            float s = 0.f;
-            for (uint32_t k = kp; k < p.n_ktiles; k += 4) s += __ldcg(base + static_cast<size_t>(k) * kTileRows + row);
-            s += __shfl_xor_sync(0xffffffffu, s, 8);
-            s += __shfl_xor_sync(0xffffffffu, s, 16);
-            if (kp == 0 && row < static_cast<int>(rows_here)) p.y[r0 + row] = __float2half_rn(s);
-            if (lane == 0) p.slab_count[slab] = 0u;
-        }
-    }
+    if constexpr (GEMV) finish_tile(p, t, acc, rows_here, lane);
+}
+
+// Shared memory: [decode table 64 KB][2 stage buffers per warp][read-ahead pad][mbarriers]
+template <int MPL>
+__host__ __device__ constexpr uint32_t overrun_pad() {
+    // a lane reads at most 4 + 3 bytes per symbol of a tile, 32 lanes apart,
+    // plus one byte row of read-ahead
+    return (32u * (5u + 3u * kTileRows * MPL) + 127u) & ~127u;
 }
 
 template <int MPL, int GPL, bool GEMV>
@@ -314,9 +414,9 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int W = blockDim.x >> 5;
-    const uint32_t bufs = smem_addr(smem);
-    const uint32_t* table = reinterpret_cast<const uint32_t*>(smem + 2 * W * p.buf_bytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 2 * W * p.buf_bytes + kTableBytes);
+    const uint32_t sbase = smem_addr(smem);  // the decode table's shared-window address
+    const uint32_t bufs_off = kTableBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + bufs_off + 2 * W * p.buf_bytes + overrun_pad<MPL>());
     const uint32_t table_bar = smem_addr(bars + 2 * W);
     const bool constant = p.flags & ECQ_FLAG_CONSTANT;
 
@@ -329,9 +429,8 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
         mbar_expect_tx(table_bar, kTableBytes);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-            bulk_copy_g2s(smem_addr(table) + i * (kTableBytes / 4),
-                          reinterpret_cast<const uint8_t*>(p.dec_table) + i * (kTableBytes / 4), kTableBytes / 4,
-                          table_bar);
+            bulk_copy_g2s(sbase + i * (kTableBytes / 4), reinterpret_cast<const uint8_t*>(p.dec_table) + i * (kTableBytes / 4),
+                          kTableBytes / 4, table_bar);
     }
 
     // contiguous run of tiles for this warp
@@ -340,7 +439,7 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
     const uint32_t t_begin = static_cast<uint32_t>(gw * p.n_tiles / GW);
     const uint32_t t_end = static_cast<uint32_t>((gw + 1) * p.n_tiles / GW);
     const uint32_t my_bar0 = smem_addr(bars + 2 * warp);
-    const uint32_t my_buf0 = bufs + 2 * warp * p.buf_bytes;
+    const uint32_t my_buf0 = bufs_off + 2 * warp * p.buf_bytes;  // offset in smem
 
     auto issue = [&](uint32_t t, int stage) {
         const uint32_t off = p.tile_offset[t];
@@ -353,7 +452,7 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
         }
         const uint32_t bar = my_bar0 + 8 * stage;
         mbar_expect_tx(bar, bytes);
-        if (bytes) bulk_copy_g2s(my_buf0 + stage * p.buf_bytes, p.data + off, bytes, bar);
+        if (bytes) bulk_copy_g2s(sbase + my_buf0 + stage * p.buf_bytes, p.data + off, bytes, bar);
     };
 
     if (lane == 0 && t_begin < t_end) issue(t_begin, 0);
@@ -377,11 +476,12 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
             break;
         }
         if (stage) phase1 ^= 1; else phase0 ^= 1;
-        const uint32_t buf = 2 * warp * p.buf_bytes + stage * p.buf_bytes;  // offset within smem
+        uint32_t buf = sbase + my_buf0 + stage * p.buf_bytes;
+        asm volatile("" : "+r"(buf)::"memory");  // keep this tile's byte loads after its wait
         if (constant)
-            process_tile<MPL, GPL, GEMV, true>(p, t, buf, table, smem, lane);
+            process_tile<MPL, GPL, GEMV, true>(p, t, buf, sbase, lane);
         else
-            process_tile<MPL, GPL, GEMV, false>(p, t, buf, table, smem, lane);
+            process_tile<MPL, GPL, GEMV, false>(p, t, buf, sbase, lane);
     }
     // never leave a bulk copy in flight when exiting after a timeout
     if (!ok && t_begin < t_end) {
@@ -459,7 +559,8 @@ int32_t shape_for(const ecq_matrix_view* m, bool gemv, LaunchShape* ls) {
     uint32_t buf = (m->max_tile_bytes + 127u) & ~127u;
     if (buf < 128) buf = 128;
     const int bar_bytes = 8 * (2 * 32 + 1);
-    int warps = static_cast<int>((kMaxSmem - kTableBytes - bar_bytes) / (2 * static_cast<int64_t>(buf)));
+    const int pad = static_cast<int>((32u * (5u + 3u * kTileRows * static_cast<uint32_t>(mpl)) + 127u) & ~127u);
+    int warps = static_cast<int>((kMaxSmem - kTableBytes - pad - bar_bytes) / (2 * static_cast<int64_t>(buf)));
     if (warps > 32) warps = 32;
     if (warps < 1) return ECQ_ERR_UNSUPPORTED;
     ls->mpl = mpl;
@@ -467,7 +568,7 @@ int32_t shape_for(const ecq_matrix_view* m, bool gemv, LaunchShape* ls) {
     ls->warps = warps;
     ls->ctas = sm_count_cached();
     ls->buf_bytes = buf;
-    ls->smem = static_cast<size_t>(2 * warps) * buf + kTableBytes + 8 * (2 * warps + 1);
+    ls->smem = static_cast<size_t>(2 * warps) * buf + kTableBytes + pad + 8 * (2 * warps + 1);
     return ECQ_OK;
 }
 

@@ -140,7 +140,7 @@ int32_t ecq_build_decode_table(const uint32_t* freq, uint32_t* entries, uint32_t
         for (uint32_t k = 0; k < f; ++k) {
             const uint32_t slot = cum + k;
             const uint32_t ff = (f == kProbScale) ? 0u : f;  // unused when constant
-            entries[slot] = static_cast<uint32_t>(s) | (ff << 4) | (k << 18);
+            entries[slot] = k | (static_cast<uint32_t>(s) << 14) | (ff << 18);
         }
         cum += f;
     }

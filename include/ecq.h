@@ -97,7 +97,8 @@ int32_t ecq_version(void);
  * remainder goes to the largest, and *normaliser = ECQ_NORMALISER_CLAMPED. */
 int32_t ecq_table_from_counts(const uint64_t *counts, uint32_t *freq, int32_t *normaliser);
 
-/* 16384 packed decode entries {sym:4 | freq:14 | slot-cumfreq:14} for a
+/* 16384 packed decode entries, entry[slot] = (slot - cumfreq[s])
+ * | s << 14 | freq[s] << 18 with s = sym_table[slot], for a
  * frequency table summing to 16384. Replaces the sym_table/freq/cumfreq
  * triple the reference's kernels read (src/rans.py:51-58,
  * src/metal_interleaved.py:52-117). */

@@ -111,10 +111,11 @@ def test_gemv_deterministic_and_workspace_reusable():
 
 
 def test_constant_matrix():
-    sym = np.full((24, 512), 11, dtype=np.uint8)
-    t = ecq.RANSTable.from_symbols(sym)  # reference normaliser gives 16384 to the one symbol
+    # > 16384 copies of one symbol: the reference normaliser gives it all 16384 slots
+    sym = np.full((40, 512), 11, dtype=np.uint8)
+    t = ecq.RANSTable.from_symbols(sym)
     assert t.freq.max() == 16384
-    sc = syn.group_scales(24, 512, 128)
+    sc = syn.group_scales(40, 512, 128)
     x = syn.activations(1, 512)
     m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, t, group_size=128), group_size=128)
     assert np.array_equal(m.decode().cpu().numpy(), sym)

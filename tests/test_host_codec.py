@@ -74,9 +74,9 @@ def test_decode_table_entries():
         e, flags = t.decode_table()
         assert flags == 0
         slot = np.arange(16384)
-        sym = e & 15
-        f = (e >> 4) & 16383
-        bias = e >> 18
+        sym = (e >> 14) & 15
+        f = e >> 18
+        bias = e & 16383
         assert np.array_equal(sym, t.sym_table)
         assert np.array_equal(f, t.freq[sym])
         assert np.array_equal(bias, slot - t.cumfreq[sym])
