@@ -87,16 +87,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         if (global_timer_ns() - t0 > kWaitLimitNs) return false;
     }
 }
-// 32-bit shared-window loads. Stream-byte loads stay ordered after the
-// mbarrier waits (volatile); table loads only depend on the decoded state.
+// 32-bit shared-window byte load, kept ordered after the mbarrier waits.
 __device__ __forceinline__ uint32_t lds_u8(uint32_t addr) {
     uint32_t v;
     asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
-__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
-    uint32_t v;
-    asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr));
     return v;
 }
 __device__ __forceinline__ void fence_proxy_async() {
@@ -671,3 +665,4 @@ int32_t ecq_device_info(int32_t* sm_count, int32_t* gemv_ctas, int32_t* gemv_war
 }
 
 }  // extern "C"
+
