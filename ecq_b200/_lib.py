@@ -29,6 +29,7 @@ STATUS_TIMEOUT = 2
 STATUS_BADARG = 4
 FLAG_CONSTANT = 1
 TILE_ROWS = 8
+NOALLOC_SCRATCH_BYTES = 4 << 20
 TABLE_ENTRIES = 16384
 
 # every symbol include/ecq.h declares
@@ -43,6 +44,7 @@ EXPORTS = (
     "ecq_matrix_decode",
     "ecq_gemv_workspace_bytes",
     "ecq_gemv",
+    "ecq_gemv_noalloc",
     "ecq_device_info",
 )
 
@@ -80,6 +82,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "ecq_matrix_decode": (c_int32, [POINTER(MatrixView), P, P, P]),
         "ecq_gemv_workspace_bytes": (c_int64, [POINTER(MatrixView), c_uint32]),
         "ecq_gemv": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, c_int64, P, P]),
+        "ecq_gemv_noalloc": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, P]),
         "ecq_device_info": (c_int32, [P, P, P, POINTER(MatrixView)]),
     }
     for name, (res, args) in sig.items():

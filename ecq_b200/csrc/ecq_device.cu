@@ -666,3 +666,65 @@ int32_t ecq_device_info(int32_t* sm_count, int32_t* gemv_ctas, int32_t* gemv_war
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// Fused GEMV on library-owned scratch: for callers that cannot allocate.
+//
+// ecq_gemv needs a few bytes of device workspace per tile. Most callers pass
+// a buffer they allocated once. Some cannot: a plugin whose host framework
+// owns the whole device-memory budget and gives its plugins none, a C host
+// with no device allocator of its own, or a latency-critical serving loop
+// that must never call cudaMalloc (it can synchronise the device and stall
+// every other stream). ecq_gemv_noalloc serves them from a fixed array that
+// lives in this library's device image instead.
+//
+// The array is a file-scope __device__ variable: every GPU that loads the
+// library holds ECQ_NOALLOC_SCRATCH_BYTES of it until the process exits.
+// From host code its name is only a host-side stand-in, never a device
+// address, so the device address is looked up once per device with
+// cudaGetSymbolAddress and cached. All calls share the one array, so two
+// calls whose kernels overlap on the GPU (different streams, or different
+// host threads) race on it and must be ordered by the caller.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_noalloc_scratch[ECQ_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+// Device address of g_noalloc_scratch on the current device; resolved on the
+// first call for that device (with that device current) and cached.
+int32_t noalloc_scratch(void** out) {
+    static std::mutex mu;
+    static void* addr[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ECQ_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return ECQ_ERR_CUDA;
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return ECQ_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t ecq_gemv_noalloc(const ecq_matrix_view* m, const void* x_f16, const void* scales_f16, void* y_f16,
+                                    uint32_t batch, uint32_t* d_status, void* stream) {
+    if (!view_ok(m) || !x_f16 || !scales_f16 || !y_f16 || !d_status || batch == 0) return ECQ_ERR_ARG;
+    const int64_t need = ecq_gemv_workspace_bytes(m, batch);
+    if (need < 0) return static_cast<int32_t>(need);
+    if (need > static_cast<int64_t>(ECQ_NOALLOC_SCRATCH_BYTES)) return ECQ_ERR_WORKSPACE;
+    void* scratch = nullptr;
+    const int32_t rc = noalloc_scratch(&scratch);
+    if (rc != ECQ_OK) return rc;
+    // The per-slab completion counters (after the per-tile partial sums) must
+    // start at zero. A finished call leaves them zero, but the array keeps
+    // whatever the last call left, including one that failed: clear them.
+    const int64_t counters = static_cast<int64_t>(m->n_tiles) * kTileRows * static_cast<int64_t>(sizeof(float));
+    if (cudaMemsetAsync(static_cast<uint8_t*>(scratch) + counters, 0, static_cast<size_t>(need - counters),
+                        static_cast<cudaStream_t>(stream)) != cudaSuccess)
+        return ECQ_ERR_CUDA;
+    return ecq_gemv(m, x_f16, scales_f16, y_f16, batch, scratch, need, d_status, stream);
+}

@@ -166,6 +166,30 @@ int64_t ecq_gemv_workspace_bytes(const ecq_matrix_view *m, uint32_t batch);
 int32_t ecq_gemv(const ecq_matrix_view *m, const void *x_f16, const void *scales_f16, void *y_f16,
                  uint32_t batch, void *workspace, int64_t workspace_bytes, uint32_t *d_status, void *stream);
 
+/* Size of the scratch array ecq_gemv_noalloc uses (4 MiB per GPU). */
+#define ECQ_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/* ecq_gemv without a caller workspace, for callers that cannot allocate
+ * device memory: a plugin whose host framework owns the whole device-memory
+ * budget, a C host with no device allocator, or a serving loop that must not
+ * call cudaMalloc because it can synchronise the device. This entry point
+ * has no counterpart in the reference; the reference's Python/Metal path
+ * allocates its buffers on every call.
+ *
+ * The workspace comes from a fixed array inside the library
+ * (ECQ_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the library until
+ * exit), so matrices whose ecq_gemv_workspace_bytes exceed it are rejected
+ * with ECQ_ERR_WORKSPACE: up to about 127K tiles (e.g. 28672 x 8192 in
+ * 8x512 tiles). Nothing is allocated, by the library or anyone else. The
+ * first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture. Every call shares the array: calls whose
+ * kernels may overlap on the GPU (other streams, other host threads) race
+ * and must be serialised by the caller. Arguments and results are those of
+ * ecq_gemv. */
+int32_t ecq_gemv_noalloc(const ecq_matrix_view *m, const void *x_f16, const void *scales_f16, void *y_f16,
+                         uint32_t batch, uint32_t *d_status, void *stream);
+
 /* Number of SMs and the persistent grid the fused kernel uses (for tests
  * and the benchmark's launch accounting). */
 int32_t ecq_device_info(int32_t *sm_count, int32_t *gemv_ctas, int32_t *gemv_warps_per_cta,
