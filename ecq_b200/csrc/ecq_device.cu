@@ -93,6 +93,11 @@ __device__ __forceinline__ uint32_t lds_u8(uint32_t addr) {
     asm volatile("ld.shared.u8 %0, [%1];" : "=r"(v) : "r"(addr));
     return v;
 }
+__device__ __forceinline__ uint16_t lds_u16(uint32_t addr) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
+}
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -161,6 +166,7 @@ struct MatrixParams {
     uint32_t n_ktiles, n_tiles;
     uint32_t buf_bytes;
     uint32_t flags;
+    uint32_t x_bytes;  // x staged in shared memory after the table (0: read x from global)
 };
 
 constexpr int kTileRows = 8;
@@ -271,11 +277,44 @@ __device__ __forceinline__ float load_row_scale(const MatrixParams& p, uint32_t 
     return __half2float(p.scales[static_cast<size_t>(row) * p.ng + (c0 + lane * GPL * 32) / p.group_size]);
 }
 
-// Finish one tile of the GEMV: reduce the lane partials over the warp,
-// publish the tile's 8 row sums, and let the last tile of a row slab sum the
-// slab's partials (fixed order, so y is deterministic) and write y.
+// Row-slab completion. A tile's 8 row sums go to the workspace and lane 0
+// bumps the slab's counter with an acquire-release atomic; the warp does not
+// wait for the atomic's result: it checks it after its next tile (or at the
+// end of its run). The warp that completes a slab sums the slab's partials in
+// fixed order (y is deterministic) and writes y.
+struct PendingSlab {
+    uint32_t slab;  // 0xffffffff: nothing pending
+    uint32_t old;   // counter value before this warp's increment (lane 0)
+    int rows;
+};
+
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* addr, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+    return old;
+}
+
+__device__ __forceinline__ void complete_pending(const MatrixParams& p, PendingSlab& pend, int lane) {
+    if (pend.slab == 0xffffffffu) return;
+    const uint32_t old = __shfl_sync(0xffffffffu, pend.old, 0);
+    if (old == p.n_ktiles - 1) {
+        __threadfence();
+        const uint32_t slab = pend.slab;
+        const int row = lane & 7, kp = lane >> 3;
+        const float* base = p.partials + static_cast<size_t>(slab) * p.n_ktiles * kTileRows;
+        float s = 0.f;
+        for (uint32_t k = kp; k < p.n_ktiles; k += 4) s += __ldcg(base + static_cast<size_t>(k) * kTileRows + row);
+        s += __shfl_xor_sync(0xffffffffu, s, 8);
+        s += __shfl_xor_sync(0xffffffffu, s, 16);
+        if (kp == 0 && row < pend.rows) p.y[slab * kTileRows + row] = __float2half_rn(s);
+        if (lane == 0) p.slab_count[slab] = 0u;
+    }
+    pend.slab = 0xffffffffu;
+}
+
 __device__ __forceinline__ void finish_tile(const MatrixParams& p, uint32_t t, float (&acc)[8], int rows_here,
-                                            int lane) {
+                                            int lane, PendingSlab& pend) {
+    complete_pending(p, pend, lane);
     // short slab: move row 0 to acc[0]
 #pragma unroll 1
     for (int r = rows_here; r < kTileRows; ++r) {
@@ -283,33 +322,30 @@ __device__ __forceinline__ void finish_tile(const MatrixParams& p, uint32_t t, f
         for (int k = 0; k < kTileRows - 1; ++k) acc[k] = acc[k + 1];
         acc[kTileRows - 1] = 0.f;
     }
-    const uint32_t slab = t / p.n_ktiles;
-    const uint32_t r0 = slab * kTileRows;
     const float v = transpose_reduce8(acc, lane);
-    if ((lane & 3) == 0) p.partials[static_cast<size_t>(t) * kTileRows + reduce_row_of_lane(lane)] = v;
-    __threadfence();
-    __syncwarp();
+    // lane 4*b2 + 8*b3 + 16*b4 holds row 4*b4 + 2*b3 + b2
+    float rv[kTileRows];
+#pragma unroll
+    for (int r = 0; r < kTileRows; ++r)
+        rv[r] = __shfl_sync(0xffffffffu, v, ((r >> 2) & 1) * 16 + ((r >> 1) & 1) * 8 + (r & 1) * 4);
+    const uint32_t slab = t / p.n_ktiles;
     uint32_t old = 0;
-    if (lane == 0) old = atomicAdd(p.slab_count + slab, 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == p.n_ktiles - 1) {
-        __threadfence();
-        const int row = lane & 7, kp = lane >> 3;
-        const float* base = p.partials + static_cast<size_t>(slab) * p.n_ktiles * kTileRows;
-        float s = 0.f;
-        for (uint32_t k = kp; k < p.n_ktiles; k += 4) s += __ldcg(base + static_cast<size_t>(k) * kTileRows + row);
-        s += __shfl_xor_sync(0xffffffffu, s, 8);
-        s += __shfl_xor_sync(0xffffffffu, s, 16);
-        if (kp == 0 && row < rows_here) p.y[r0 + row] = __float2half_rn(s);
-        if (lane == 0) p.slab_count[slab] = 0u;
+    if (lane == 0) {
+        float4* dst = reinterpret_cast<float4*>(p.partials + static_cast<size_t>(t) * kTileRows);
+        dst[0] = make_float4(rv[0], rv[1], rv[2], rv[3]);
+        dst[1] = make_float4(rv[4], rv[5], rv[6], rv[7]);
+        old = atom_add_acq_rel(p.slab_count + slab, 1u);
     }
+    pend.slab = slab;
+    pend.old = old;
+    pend.rows = rows_here;
 }
 
 // Decode one tile (buf = offset of its bytes in shared memory) and either
 // accumulate its GEMV contribution or store its symbols.
 template <int MPL, int GPL, bool GEMV, bool CONSTANT>
 __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, uint32_t buf, uint32_t tb,
-                                             int lane) {
+                                             int lane, PendingSlab& pend) {
     constexpr int NSG = MPL / GPL;  // scale groups per tile row
     const uint32_t slab = t / p.n_ktiles;
     const uint32_t kt = t - slab * p.n_ktiles;
@@ -328,7 +364,12 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
     float sc = 0.f;
     if constexpr (GEMV) {
 #pragma unroll
-        for (int m = 0; m < MPL; ++m) xs[m] = __half2float(p.x[c0 + 32 * m + lane]) * 6.103515625e-05f;
+        for (int m = 0; m < MPL; ++m) {
+            // x is staged in shared memory right after the table (when it fits)
+            const float xv = p.x_bytes ? __half2float(__ushort_as_half(lds_u16(tb + kTableBytes + 2u * (c0 + 32 * m + lane))))
+                                       : __half2float(p.x[c0 + 32 * m + lane]);
+            xs[m] = xv * 6.103515625e-05f;
+        }
 #pragma unroll
         for (int r = 0; r < kTileRows; ++r) acc[r] = 0.f;
         sc = load_row_scale<NSG, GPL>(p, r0, c0, lane);
@@ -391,7 +432,7 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
         if (len != 4u) atomicOr(p.status, ECQ_STATUS_CORRUPT);
     }
 
-    if constexpr (GEMV) finish_tile(p, t, acc, rows_here, lane);
+    if constexpr (GEMV) finish_tile(p, t, acc, rows_here, lane, pend);
 }
 
 // Shared memory: [decode table 64 KB][2 stage buffers per warp][read-ahead pad][mbarriers]
@@ -409,7 +450,7 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
     const int warp = threadIdx.x >> 5;
     const int W = blockDim.x >> 5;
     const uint32_t sbase = smem_addr(smem);  // the decode table's shared-window address
-    const uint32_t bufs_off = kTableBytes;
+    const uint32_t bufs_off = kTableBytes + ((p.x_bytes + 127u) & ~127u);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + bufs_off + 2 * W * p.buf_bytes + overrun_pad<MPL>());
     const uint32_t table_bar = smem_addr(bars + 2 * W);
     const bool constant = p.flags & ECQ_FLAG_CONSTANT;
@@ -420,11 +461,12 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        mbar_expect_tx(table_bar, kTableBytes);
+        mbar_expect_tx(table_bar, kTableBytes + p.x_bytes);
 #pragma unroll
         for (int i = 0; i < 4; ++i)
             bulk_copy_g2s(sbase + i * (kTableBytes / 4), reinterpret_cast<const uint8_t*>(p.dec_table) + i * (kTableBytes / 4),
                           kTableBytes / 4, table_bar);
+        if (p.x_bytes) bulk_copy_g2s(sbase + kTableBytes, p.x, p.x_bytes, table_bar);
     }
 
     // contiguous run of tiles for this warp
@@ -454,6 +496,7 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
     if (!ok && lane == 0) atomicOr(p.status, ECQ_STATUS_TIMEOUT);
 
     uint32_t phase0 = 0, phase1 = 0;
+    PendingSlab pend{0xffffffffu, 0u, 0};
     for (uint32_t t = t_begin; ok && t < t_end; ++t) {
         const int stage = (t - t_begin) & 1;
         if (t + 1 < t_end) {
@@ -473,10 +516,11 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
         uint32_t buf = sbase + my_buf0 + stage * p.buf_bytes;
         asm volatile("" : "+r"(buf)::"memory");  // keep this tile's byte loads after its wait
         if (constant)
-            process_tile<MPL, GPL, GEMV, true>(p, t, buf, sbase, lane);
+            process_tile<MPL, GPL, GEMV, true>(p, t, buf, sbase, lane, pend);
         else
-            process_tile<MPL, GPL, GEMV, false>(p, t, buf, sbase, lane);
+            process_tile<MPL, GPL, GEMV, false>(p, t, buf, sbase, lane, pend);
     }
+    if constexpr (GEMV) complete_pending(p, pend, lane);
     // never leave a bulk copy in flight when exiting after a timeout
     if (!ok && t_begin < t_end) {
         mbar_wait(my_bar0, phase0);
@@ -529,6 +573,7 @@ struct LaunchShape {
     int mpl, gpl, warps, ctas;
     uint32_t buf_bytes;
     size_t smem;
+    uint32_t x_bytes;
 };
 
 int32_t shape_for(const ecq_matrix_view* m, bool gemv, LaunchShape* ls) {
@@ -554,7 +599,11 @@ int32_t shape_for(const ecq_matrix_view* m, bool gemv, LaunchShape* ls) {
     if (buf < 128) buf = 128;
     const int bar_bytes = 8 * (2 * 32 + 1);
     const int pad = static_cast<int>((32u * (5u + 3u * kTileRows * static_cast<uint32_t>(mpl)) + 127u) & ~127u);
-    int warps = static_cast<int>((kMaxSmem - kTableBytes - pad - bar_bytes) / (2 * static_cast<int64_t>(buf)));
+    // stage x in shared memory when it leaves room for at least 16 warps
+    uint32_t xb = gemv ? m->cols * 2u : 0u;
+    if (xb > static_cast<uint32_t>(kMaxSmem - kTableBytes - pad - bar_bytes) - 16u * 2u * buf) xb = 0;
+    const int xpad = static_cast<int>((xb + 127u) & ~127u);
+    int warps = static_cast<int>((kMaxSmem - kTableBytes - xpad - pad - bar_bytes) / (2 * static_cast<int64_t>(buf)));
     if (warps > 32) warps = 32;
     if (warps < 1) return ECQ_ERR_UNSUPPORTED;
     ls->mpl = mpl;
@@ -562,7 +611,8 @@ int32_t shape_for(const ecq_matrix_view* m, bool gemv, LaunchShape* ls) {
     ls->warps = warps;
     ls->ctas = sm_count_cached();
     ls->buf_bytes = buf;
-    ls->smem = static_cast<size_t>(2 * warps) * buf + kTableBytes + pad + 8 * (2 * warps + 1);
+    ls->smem = static_cast<size_t>(2 * warps) * buf + kTableBytes + xpad + pad + 8 * (2 * warps + 1);
+    ls->x_bytes = xb;
     return ECQ_OK;
 }
 
@@ -589,6 +639,8 @@ int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, cons
     p.n_tiles = m->n_tiles;
     p.buf_bytes = ls.buf_bytes;
     p.flags = m->flags;
+    // x staged by bulk copy needs a 16-byte aligned address
+    p.x_bytes = (gemv && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) ? ls.x_bytes : 0u;
     if (gemv) {
         p.partials = static_cast<float*>(workspace);
         p.slab_count = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) +
