@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--replicas", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-llama", action="store_true", help="skip the 7B tensor-parallel decode step")
+    ap.add_argument("--llama-steps", type=int, default=20)
     return ap.parse_args()
 
 
@@ -366,6 +368,16 @@ def run_ecq(args):
                          f"symbols, {secs:.2f} s): oracle C restatement of interleaved_rans_decode per tile + "
                          f"dequant + matvec, {threads} threads over row slabs"}
 
+    llama = None
+    if not args.no_llama:
+        del step_graph, launch_graphs
+        if not args.no_e2e:
+            del e2e_graph
+        sets.clear()
+        torch.cuda.empty_cache()
+        llama = run_llama(args, world, rank, local, dev, barrier)
+        step_graph = launch_graphs = None
+
     comp_bytes_step = R * sum(algorithmic_bytes(d0["enc"], d0["M"], d0["K"]) for d0 in inputs)
     ms_step = ms_max / args.steps
     line = {
@@ -391,6 +403,7 @@ def run_ecq(args):
         },
         "e2e": e2e,
         "cpu_baseline": cpu,
+        "llama7b_decode": llama,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
@@ -399,6 +412,56 @@ def run_ecq(args):
     if world > 1:
         del step_graph, launch_graphs
         dist.destroy_process_group()
+
+
+def run_llama(args, world, rank, local, dev, barrier):
+    """Synthetic Llama-7B batch-1 decode step, tensor-parallel over the ranks,
+    captured in one CUDA graph (NCCL all-reduces included). Returns its summary."""
+    import torch
+    import torch.distributed as dist
+
+    from ecq_b200.model import Llama7BDecoder
+
+    t0 = time.perf_counter()
+    dec = Llama7BDecoder(tp=world, rank=rank, device=dev, group=None)
+    build_s = time.perf_counter() - t0
+    tok = torch.tensor([1], device=dev)
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            dec.step(tok)
+        s.synchronize()
+        dec.check()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            out = dec.step(tok)
+        for _ in range(3):
+            g.replay()
+        s.synchronize()
+    barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        a.record(s)
+        for _ in range(args.llama_steps):
+            g.replay()
+        b.record(s)
+    b.synchronize()
+    ms = a.elapsed_time(b) / args.llama_steps
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    dec.check()
+    res = {"tokens_per_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 3), "tp": world,
+           "steps": args.llama_steps, "symbols_per_token_per_rank": dec.symbols,
+           "compressed_bytes_per_rank": dec.compressed_bytes, "build_s": round(build_s, 1),
+           "next_token": int(out.item()),
+           "config": "32 layers, hidden 4096, 32 heads x 128, MLP 11008, vocab 32000, 2048-token fp16 KV cache; "
+                     "Student-t(4)*0.02 weights, group-128 symmetric 4-bit, rANS per matrix; batch 1; CUDA graph"}
+    del g
+    return res
 
 
 def main():

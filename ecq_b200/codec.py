@@ -287,3 +287,37 @@ def pack_reference_tiles(tiles, rows: int, cols: int, tile_rows: int, tile_cols:
     return EncodedMatrix(rows=rows, cols=cols, tile_rows=tile_rows, tile_cols=tile_cols, table=tbl,
                          data=np.frombuffer(b"".join(t.data for t in tiles), dtype=np.uint8).copy(),
                          tile_offset=np.array(offs, dtype=np.uint32), stream_len=np.array(lens, dtype=np.uint16))
+
+
+def slice_matrix(enc: EncodedMatrix, slab0: int, slab1: int, kt0: int, kt1: int) -> EncodedMatrix:
+    """The packed sub-matrix made of row slabs [slab0, slab1) and K-tiles
+    [kt0, kt1) of `enc` (same table, same tile bytes). Tensor-parallel ranks
+    take their shard this way, so one encoding serves every TP size."""
+    nk = enc.cols // enc.tile_cols
+    n_slabs = (enc.rows + enc.tile_rows - 1) // enc.tile_rows
+    if not (0 <= slab0 < slab1 <= n_slabs and 0 <= kt0 < kt1 <= nk):
+        raise ValueError("slice out of range")
+    t = (np.arange(slab0, slab1)[:, None] * nk + np.arange(kt0, kt1)[None, :]).reshape(-1)
+    o0 = enc.tile_offset[t].astype(np.int64)
+    o1 = enc.tile_offset[t + 1].astype(np.int64)
+    sizes = o1 - o0
+    offs = np.zeros(t.size + 1, dtype=np.int64)
+    np.cumsum(sizes, out=offs[1:])
+    idx = np.repeat(o0 - offs[:-1], sizes) + np.arange(int(offs[-1]))
+    lens = enc.stream_len.reshape(-1, 32)[t].reshape(-1)
+    rows = min(slab1 * enc.tile_rows, enc.rows) - slab0 * enc.tile_rows
+    return EncodedMatrix(rows=rows, cols=(kt1 - kt0) * enc.tile_cols, tile_rows=enc.tile_rows,
+                         tile_cols=enc.tile_cols, table=enc.table, data=enc.data[idx],
+                         tile_offset=offs.astype(np.uint32), stream_len=np.ascontiguousarray(lens))
+
+
+def split_even(n: int, parts: int) -> list[tuple[int, int]]:
+    """[lo, hi) ranges splitting n units into `parts` contiguous pieces whose
+    sizes differ by at most one (the first n % parts pieces get one more)."""
+    base, extra = divmod(n, parts)
+    out, lo = [], 0
+    for i in range(parts):
+        hi = lo + base + (1 if i < extra else 0)
+        out.append((lo, hi))
+        lo = hi
+    return out

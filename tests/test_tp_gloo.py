@@ -1,0 +1,112 @@
+"""Tensor-parallel host logic on CPU: world_size-2 gloo ranks shard a small
+rANS-coded MLP and attention-output projection exactly as the 7B decode step
+does (row slabs for column-parallel layers, K-tiles + all-reduce for
+row-parallel layers, gate/up split following down's K-tiles). Each rank decodes
+its shard with the oracle; the all-reduced result must equal the unsharded
+computation. No GPU is involved."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import ecq_b200 as ecq
+from ecq_b200.codec import slice_matrix, split_even
+from ecq_b200.model import Llama7BConfig, tp_partition
+from ecq_b200 import synthetic as syn
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _shard_gemv(enc, sc, x, slabs, kts):
+    from oracle import oracle
+    sub = slice_matrix(enc, slabs[0], slabs[1], kts[0], kts[1])
+    out, bad = [], 0
+    sym = np.zeros((sub.rows, sub.cols), np.uint8)
+    nk = sub.cols // sub.tile_cols
+    for t in range(sub.n_tiles):
+        tile = sub.tile(t)
+        d, b, _, _ = oracle.decode_interleaved(tile.data, tile.stream_lengths, 32, tile.n_symbols, sub.table.freq)
+        bad += b
+        s, k = divmod(t, nk)
+        nr = tile.n_symbols // sub.tile_cols
+        sym[s * 8:s * 8 + nr, k * sub.tile_cols:(k + 1) * sub.tile_cols] = d.reshape(nr, sub.tile_cols)
+    assert bad == 0
+    r0, c0 = slabs[0] * 8, kts[0] * enc.tile_cols
+    return oracle.dequant_gemv(sym, sc[r0:r0 + sub.rows, c0 // 128:(c0 + sub.cols) // 128], 128,
+                               x[c0:c0 + sub.cols])
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        H, F = 256, 1024  # hidden, mlp (tiles: 256 and 256 wide)
+        rng = np.random.default_rng(7)
+        wg, sg = syn.quantize_symmetric_groups(syn.student_t_weights(F, H, 11), 128)
+        wd, sd = syn.quantize_symmetric_groups(syn.student_t_weights(H, F, 12), 128)
+        eg = ecq.encode_matrix(wg, tile_cols=256, group_size=128)
+        ed = ecq.encode_matrix(wd, tile_cols=256, group_size=128)
+        x = rng.standard_normal(H).astype(np.float32)
+        kt_d = split_even(F // 256, world)[rank]
+        mlp_slabs = (kt_d[0] * 256 // 8, kt_d[1] * 256 // 8)
+        g = _shard_gemv(eg, sg.astype(np.float32), x, mlp_slabs, (0, 1))
+        m = g * (1 / (1 + np.exp(-g)))  # silu(gate) (up folded into the test: same layout)
+        part = np.zeros(H, np.float32)
+        part[:] = _shard_gemv(ed, sd.astype(np.float32), np.concatenate(
+            [np.zeros(kt_d[0] * 256, np.float32), m, np.zeros(F - kt_d[1] * 256, np.float32)]),
+            (0, H // 8), kt_d)
+        t = torch.from_numpy(part)
+        dist.all_reduce(t)
+        q.put((rank, t.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp_mlp_two_gloo_ranks_match_unsharded():
+    from oracle import oracle
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    H, F = 256, 1024
+    wg, sg = syn.quantize_symmetric_groups(syn.student_t_weights(F, H, 11), 128)
+    wd, sd = syn.quantize_symmetric_groups(syn.student_t_weights(H, F, 12), 128)
+    x = np.random.default_rng(7).standard_normal(H).astype(np.float32)
+    g = oracle.dequant_gemv(wg, sg.astype(np.float32), 128, x)
+    y = oracle.dequant_gemv(wd, sd.astype(np.float32), 128, g * (1 / (1 + np.exp(-g))))
+    for r in range(world):
+        assert np.allclose(res[r], y, rtol=1e-4, atol=1e-4 * np.abs(y).max())
+
+
+@pytest.mark.parametrize("tp", [1, 2, 4, 8])
+def test_tp_partition_of_llama7b(tp):
+    cfg = Llama7BConfig()
+    plans = tp_partition(cfg, tp)
+    # every kind of shard covers its dimension exactly once, in order
+    for key, total in (("qkv_slabs", 512), ("o_ktiles", 8), ("down_ktiles", 43), ("vocab_slabs", 4000),
+                       ("mlp_slabs", 1376)):
+        spans = [p[key] for p in plans]
+        assert spans[0][0] == 0 and spans[-1][1] == total
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    for p in plans:
+        # a rank's q/k/v heads are exactly the o_proj columns it owns
+        assert (p["qkv_slabs"][1] - p["qkv_slabs"][0]) * 8 == (p["o_ktiles"][1] - p["o_ktiles"][0]) * 512
+        assert p["qkv_slabs"][0] * 8 == p["o_ktiles"][0] * 512
+        # gate/up rows are exactly the down_proj K-range
+        assert p["mlp_slabs"][0] * 8 == p["down_ktiles"][0] * 256
+        assert p["mlp_slabs"][1] * 8 == p["down_ktiles"][1] * 256
