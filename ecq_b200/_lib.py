@@ -32,7 +32,7 @@ TILE_ROWS = 8
 NOALLOC_SCRATCH_BYTES = 4 << 20
 TABLE_ENTRIES = 16384
 
-# every symbol include/ecq.h declares
+# every function include/*.h declares
 EXPORTS = (
     "ecq_version",
     "ecq_table_from_counts",
@@ -46,6 +46,9 @@ EXPORTS = (
     "ecq_gemv",
     "ecq_gemv_noalloc",
     "ecq_device_info",
+    "ecq_add_rmsnorm_f16",
+    "ecq_rope_kv_f16",
+    "ecq_silu_mul_f16",
 )
 
 
@@ -84,6 +87,9 @@ def _declare(L: ctypes.CDLL) -> None:
         "ecq_gemv": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, c_int64, P, P]),
         "ecq_gemv_noalloc": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, P]),
         "ecq_device_info": (c_int32, [P, P, P, POINTER(MatrixView)]),
+        "ecq_add_rmsnorm_f16": (c_int32, [P, P, P, P, P, c_int32, c_int32, ctypes.c_float, P]),
+        "ecq_rope_kv_f16": (c_int32, [P, P, P, P, P, P, P, c_int32, c_int32, c_int64, P]),
+        "ecq_silu_mul_f16": (c_int32, [P, P, c_int32, c_int32, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -321,3 +321,28 @@ def split_even(n: int, parts: int) -> list[tuple[int, int]]:
         out.append((lo, hi))
         lo = hi
     return out
+
+
+def concat_rows(parts) -> EncodedMatrix:
+    """Stack packed matrices that share columns, tile width and table into
+    one (e.g. a fused q|k|v projection): their tiles are concatenated in order.
+    Every part but the last must have a whole number of 8-row slabs."""
+    parts = list(parts)
+    p0 = parts[0]
+    for q in parts:
+        if (q.cols, q.tile_cols, q.tile_rows) != (p0.cols, p0.tile_cols, p0.tile_rows):
+            raise ValueError("parts differ in columns or tile shape")
+        if not np.array_equal(q.table.freq, p0.table.freq):
+            raise ValueError("parts must share one table")
+    for q in parts[:-1]:
+        if q.rows % q.tile_rows:
+            raise ValueError("only the last part may end in a short slab")
+    offs = [np.zeros(1, np.int64)]
+    base = 0
+    for q in parts:
+        offs.append(q.tile_offset[1:].astype(np.int64) + base)
+        base += int(q.tile_offset[-1])
+    return EncodedMatrix(rows=sum(q.rows for q in parts), cols=p0.cols, tile_rows=p0.tile_rows,
+                         tile_cols=p0.tile_cols, table=p0.table, data=np.concatenate([q.data for q in parts]),
+                         tile_offset=np.concatenate(offs).astype(np.uint32),
+                         stream_len=np.concatenate([q.stream_len for q in parts]))

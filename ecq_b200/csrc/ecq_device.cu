@@ -265,10 +265,6 @@ __device__ __forceinline__ float transpose_reduce8(float (&v)[8], int lane) {
     return v[0];
 }
 
-__device__ __forceinline__ int reduce_row_of_lane(int lane) {
-    return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-}
-
 // Lane l < NSG holds the scale of scale-group l of this tile row (the NSG
 // groups a tile row spans); the others hold 0.
 template <int NSG, int GPL>

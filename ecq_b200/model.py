@@ -15,8 +15,11 @@ Tensor parallelism (one process per GPU, NCCL over NVLink):
     and the partial outputs are summed with one all-reduce per layer;
   * the gate/up row split follows down_proj's K-tile split, so the MLP needs
     no re-sharding; lm_head logits are all-gathered.
-Every matrix is encoded once with its global table and ranks take tile
-subsets (codec.slice_matrix), so one encoding serves TP = 1/2/4/8.
+Each matrix (q|k|v and gate|up as fused projections sharing one table) is
+encoded with its global table and every rank encodes exactly the tiles of its
+shard, which are the same tiles whatever the TP size. A layer launches 4
+fused GEMVs, 3 glue kernels (ecq_glue.h), attention and, with TP, 2
+all-reduces.
 """
 from __future__ import annotations
 
@@ -27,7 +30,9 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from .codec import RANSTable, encode_matrix, slice_matrix, split_even, choose_tile_cols
+from . import _lib
+from ._lib import check, lib
+from .codec import RANSTable, concat_rows, encode_matrix, split_even, choose_tile_cols
 from .device import DeviceMatrix
 from .ops import rans_gemv
 
@@ -77,21 +82,22 @@ class ShardedLinear:
         return rans_gemv(x, self.m, self.scales)
 
 
-def _encode_shard(q_full: torch.Tensor, sc_full: torch.Tensor, slabs: tuple[int, int], ktiles: tuple[int, int] | None,
-                  tile_cols: int, device) -> ShardedLinear:
-    M, K = q_full.shape
-    counts = torch.bincount(q_full.reshape(-1), minlength=16).cpu().numpy()
-    table = RANSTable.from_counts(counts)
-    nk = K // tile_cols
-    k0, k1 = ktiles if ktiles is not None else (0, nk)
-    s0, s1 = slabs
-    r0, r1 = s0 * 8, min(s1 * 8, M)
-    c0, c1 = k0 * tile_cols, k1 * tile_cols
-    block = q_full[r0:r1, c0:c1].contiguous().cpu().numpy()
-    enc = encode_matrix(block, table, tile_cols=tile_cols, group_size=GROUP)
+def _encode_shards(parts, table: RANSTable, tile_cols: int, device) -> ShardedLinear:
+    """Encode the row blocks `parts` = [(symbols, scales, (r0, r1), (c0, c1)), ...]
+    with one shared table and stack them into one packed matrix."""
+    encs, scs = [], []
+    for q_full, sc_full, (r0, r1), (c0, c1) in parts:
+        block = q_full[r0:r1, c0:c1].contiguous().cpu().numpy()
+        encs.append(encode_matrix(block, table, tile_cols=tile_cols, group_size=GROUP))
+        scs.append(sc_full[r0:r1, c0 // GROUP:c1 // GROUP])
+    enc = concat_rows(encs) if len(encs) > 1 else encs[0]
     m = DeviceMatrix.from_encoded(enc, group_size=GROUP, device=device)
-    scales = sc_full[r0:r1, c0 // GROUP:c1 // GROUP].contiguous().to(device)
-    return ShardedLinear(m, scales)
+    return ShardedLinear(m, torch.cat(scs, dim=0).contiguous().to(device))
+
+
+def _table_of(*mats: torch.Tensor) -> RANSTable:
+    counts = sum(torch.bincount(q.reshape(-1), minlength=16) for q in mats)
+    return RANSTable.from_counts(counts.cpu().numpy())
 
 
 class Llama7BDecoder:
@@ -123,28 +129,35 @@ class Llama7BDecoder:
         self.seed = seed
         s = seed
         self.layers = []
+        hr = (head_slabs[0] * 8, head_slabs[1] * 8)
+        mr = (mlp_slabs[0] * 8, mlp_slabs[1] * 8)
         for li in range(cfg.layers):
             lw = {}
+            W = {}
             for name, (M, K) in (("q", (H, H)), ("k", (H, H)), ("v", (H, H)), ("o", (H, H)),
                                  ("gate", (cfg.mlp, H)), ("up", (cfg.mlp, H)), ("down", (H, cfg.mlp))):
-                q, sc = quantized_student_t(M, K, seed=s, device=self.dev)
+                W[name] = quantized_student_t(M, K, seed=s, device=self.dev)
                 s += 1
-                if name in ("q", "k", "v"):
-                    lw[name] = _encode_shard(q, sc, head_slabs, None, tc_h, self.dev)
-                elif name == "o":
-                    lw[name] = _encode_shard(q, sc, (0, H // 8), kt_o, tc_h, self.dev)
-                elif name in ("gate", "up"):
-                    lw[name] = _encode_shard(q, sc, mlp_slabs, None, tc_h, self.dev)
-                else:
-                    lw[name] = _encode_shard(q, sc, (0, H // 8), kt_d, tc_m, self.dev)
-                self.compressed_bytes += lw[name].m.compressed_bytes
-                self.symbols += lw[name].m.rows * lw[name].m.cols
-                del q, sc
+            t_qkv = _table_of(W["q"][0], W["k"][0], W["v"][0])
+            lw["qkv"] = _encode_shards([(W[n][0], W[n][1], hr, (0, H)) for n in ("q", "k", "v")], t_qkv, tc_h,
+                                       self.dev)
+            lw["o"] = _encode_shards([(W["o"][0], W["o"][1], (0, H), (kt_o[0] * tc_h, kt_o[1] * tc_h))],
+                                     _table_of(W["o"][0]), tc_h, self.dev)
+            t_gu = _table_of(W["gate"][0], W["up"][0])
+            lw["gate_up"] = _encode_shards([(W[n][0], W[n][1], mr, (0, H)) for n in ("gate", "up")], t_gu, tc_h,
+                                           self.dev)
+            lw["down"] = _encode_shards([(W["down"][0], W["down"][1], (0, H), (kt_d[0] * tc_m, kt_d[1] * tc_m))],
+                                        _table_of(W["down"][0]), tc_m, self.dev)
+            del W
+            for k in ("qkv", "o", "gate_up", "down"):
+                self.compressed_bytes += lw[k].m.compressed_bytes
+                self.symbols += lw[k].m.rows * lw[k].m.cols
             lw["ln1"] = torch.ones(H, device=self.dev, dtype=torch.float16)
             lw["ln2"] = torch.ones(H, device=self.dev, dtype=torch.float16)
             self.layers.append(lw)
         q, sc = quantized_student_t(cfg.vocab, H, seed=s, device=self.dev)
-        self.lm_head = _encode_shard(q, sc, vocab_slabs, None, tc_h, self.dev)
+        vr = (vocab_slabs[0] * 8, min(vocab_slabs[1] * 8, cfg.vocab))
+        self.lm_head = _encode_shards([(q, sc, vr, (0, H))], _table_of(q), tc_h, self.dev)
         self.compressed_bytes += self.lm_head.m.compressed_bytes
         self.symbols += self.lm_head.m.rows * self.lm_head.m.cols
         del q, sc
@@ -163,13 +176,13 @@ class Llama7BDecoder:
         self.logits = torch.empty(tp, max(self.vocab_sizes), device=self.dev, dtype=torch.float16)
 
     # -- glue ------------------------------------------------------------------
-    def _rms(self, h: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-        hf = h.float()
-        return (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + self.cfg.eps)).to(torch.float16) * w
-
-    def _rope(self, t: torch.Tensor) -> torch.Tensor:
-        a, b = t[..., 0::2], t[..., 1::2]
-        return torch.stack((a * self.cos - b * self.sin, a * self.sin + b * self.cos), dim=-1).flatten(-2)
+    def _add_rms(self, h: torch.Tensor, d: torch.Tensor | None, w: torch.Tensor) -> torch.Tensor:
+        """h += d (in place, when d is given); returns rmsnorm(h) * w."""
+        y = torch.empty_like(h)
+        check(lib().ecq_add_rmsnorm_f16(h.data_ptr(), d.data_ptr() if d is not None else None, w.data_ptr(),
+                                        h.data_ptr(), y.data_ptr(), h.shape[0], h.shape[1], self.cfg.eps,
+                                        torch.cuda.current_stream(self.dev).cuda_stream), "add_rmsnorm")
+        return y
 
     def _all_reduce(self, t: torch.Tensor) -> torch.Tensor:
         if self.tp > 1:
@@ -184,23 +197,30 @@ class Llama7BDecoder:
         """One batch-1 decode step returning the full fp16 logits [vocab]."""
         cfg = self.cfg
         D, nh = cfg.head_dim, self.local_heads
-        h = self.embed[token].reshape(1, cfg.hidden)
+        L = nh * D
+        F = self.mlp_rows[1] - self.mlp_rows[0]
+        stream = torch.cuda.current_stream(self.dev).cuda_stream
+        h = self.embed[token].reshape(1, cfg.hidden).clone()
+        d = None
         for li, lw in enumerate(self.layers):
-            a = self._rms(h, lw["ln1"])
-            q = self._rope(lw["q"](a).view(nh, 1, D))
-            k = self._rope(lw["k"](a).view(nh, 1, D))
-            v = lw["v"](a).view(nh, 1, D)
-            self.kv[li, 0, :, cfg.kv_len:cfg.kv_len + 1].copy_(k)
-            self.kv[li, 1, :, cfg.kv_len:cfg.kv_len + 1].copy_(v)
-            att = torch.nn.functional.scaled_dot_product_attention(
-                q.unsqueeze(0), self.kv[li, 0].unsqueeze(0), self.kv[li, 1].unsqueeze(0))
-            o = self._all_reduce(lw["o"](att.reshape(1, nh * D)))
-            h = h + o
-            a = self._rms(h, lw["ln2"])
-            m = torch.nn.functional.silu(lw["gate"](a)) * lw["up"](a)
+            a = self._add_rms(h, d, lw["ln1"])
+            qkv = lw["qkv"](a)                      # [1, 3L]: q | k | v
+            kslot = self.kv[li, 0, :, cfg.kv_len]
+            vslot = self.kv[li, 1, :, cfg.kv_len]
+            check(lib().ecq_rope_kv_f16(qkv.data_ptr(), qkv[:, L:].data_ptr(), qkv[:, 2 * L:].data_ptr(),
+                                        kslot.data_ptr(), vslot.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(),
+                                        nh, D, (cfg.kv_len + 1) * D, stream), "rope_kv")
+            q = qkv[:, :L].reshape(1, nh, 1, D)
+            att = torch.nn.functional.scaled_dot_product_attention(q, self.kv[li, 0].unsqueeze(0),
+                                                                   self.kv[li, 1].unsqueeze(0))
+            o = self._all_reduce(lw["o"](att.reshape(1, L)))
+            a = self._add_rms(h, o, lw["ln2"])
+            gu = lw["gate_up"](a)                   # [1, 2F]: gate | up
+            m = torch.empty(1, F, device=self.dev, dtype=torch.float16)
+            check(lib().ecq_silu_mul_f16(gu.data_ptr(), m.data_ptr(), F, 1, stream), "silu_mul")
             d = self._all_reduce(lw["down"](m))
-            h = h + d
-        logits = self.lm_head(self._rms(h, self.norm)).reshape(-1)
+        a = self._add_rms(h, d, self.norm)
+        logits = self.lm_head(a).reshape(-1)
         if self.tp > 1:
             local = torch.full((self.logits.shape[1],), -65504.0, device=self.dev, dtype=torch.float16)
             local[: logits.numel()].copy_(logits)
@@ -210,7 +230,7 @@ class Llama7BDecoder:
 
     def check(self) -> None:
         for lw in self.layers:
-            for k in ("q", "k", "v", "o", "gate", "up", "down"):
+            for k in ("qkv", "o", "gate_up", "down"):
                 lw[k].m.check()
         self.lm_head.m.check()
 
@@ -232,4 +252,4 @@ def tp_partition(cfg: Llama7BConfig, tp: int) -> list[dict]:
     return plans
 
 
-__all__ = ["Llama7BConfig", "Llama7BDecoder", "tp_partition", "quantized_student_t", "math"]
+__all__ = ["Llama7BConfig", "Llama7BDecoder", "tp_partition", "quantized_student_t", "math", "_lib", "np"]

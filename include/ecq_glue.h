@@ -1,0 +1,39 @@
+/*
+ * ecq_glue.h -- element-wise steps of a batch-1 transformer decode step that
+ * sit between libecq's fused GEMVs (no counterpart in the reference, whose
+ * model glue lives in the out-of-tree MLX fork; the model structure it
+ * drives is experiments/real_model_test.py:18-113). fp16 in/out, fp32
+ * arithmetic; every launch takes a cudaStream_t (as void*) and returns 0 or
+ * a negative error.
+ */
+#ifndef ECQ_GLUE_H
+#define ECQ_GLUE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* h_out = h + d (rounded to fp16; skipped when d is NULL) and
+ * y = fp16(h_out * rsqrt(mean(h_out^2) + eps)) * w, for `rows` rows of n
+ * (n <= 12256). */
+int32_t ecq_add_rmsnorm_f16(const void *h, const void *d, const void *w, void *h_out, void *y, int32_t rows,
+                            int32_t n, float eps, void *stream);
+
+/* Rotary embedding of q (in place) and k for one position (angles cos_t /
+ * sin_t, dim/2 each, pairs (2i, 2i+1)), storing the rotated k and v into the
+ * KV cache slots k_cache / v_cache (head h at h * cache_head_stride
+ * elements). q, k, v are [heads, dim]. */
+int32_t ecq_rope_kv_f16(void *q, const void *k, const void *v, void *k_cache, void *v_cache, const void *cos_t,
+                        const void *sin_t, int32_t heads, int32_t dim, int64_t cache_head_stride, void *stream);
+
+/* m[r, c] = fp16(silu(gate[r, c])) * up[r, c] with gate_up = [rows, 2f]
+ * (gate in the first f columns, up in the next f). */
+int32_t ecq_silu_mul_f16(const void *gate_up, void *m, int32_t f, int32_t rows, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ECQ_GLUE_H */

@@ -5,13 +5,15 @@ from pathlib import Path
 
 from ecq_b200 import _lib
 
-HEADER = Path(__file__).resolve().parents[1] / "include" / "ecq.h"
+HEADERS = sorted((Path(__file__).resolve().parents[1] / "include").glob("*.h"))
 
 
 def declared_functions():
-    text = HEADER.read_text()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:int32_t|int64_t|void)\s+(ecq_\w+)\s*\(", text, flags=re.M)))
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names |= set(re.findall(r"^\s*(?:int32_t|int64_t|void)\s+(ecq_\w+)\s*\(", text, flags=re.M))
+    return sorted(names)
 
 
 def test_header_and_binding_agree():

@@ -20,6 +20,17 @@ def _dequant(q, sc):
     return (q.float() - 8.0) * sc.float().repeat_interleave(128, dim=1)
 
 
+def _rms(h, w, eps=1e-5):
+    hf = h.float()
+    return (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + eps)).to(torch.float16) * w
+
+
+def _rope(t, cos, sin):
+    a, b = t[..., 0::2].float(), t[..., 1::2].float()
+    c, s = cos.float(), sin.float()
+    return torch.stack((a * c - b * s, a * s + b * c), dim=-1).flatten(-2).to(torch.float16)
+
+
 def test_small_decoder_matches_fp32_reference():
     cfg = Llama7BConfig(layers=2, hidden=512, heads=4, head_dim=128, mlp=1024, vocab=1000, kv_len=64)
     dec = Llama7BDecoder(cfg, tp=1, seed=5)
@@ -45,19 +56,19 @@ def test_small_decoder_matches_fp32_reference():
     kv = kv0
     h = dec.embed[tok].reshape(1, 512)
     for li, lw in enumerate(W):
-        a = dec._rms(h, torch.ones(512, device="cuda", dtype=torch.float16))
-        qh = dec._rope(lin(lw["q"], a).view(4, 1, 128))
-        kh = dec._rope(lin(lw["k"], a).view(4, 1, 128))
+        a = _rms(h, torch.ones(512, device="cuda", dtype=torch.float16))
+        qh = _rope(lin(lw["q"], a).view(4, 1, 128), dec.cos, dec.sin)
+        kh = _rope(lin(lw["k"], a).view(4, 1, 128), dec.cos, dec.sin)
         vh = lin(lw["v"], a).view(4, 1, 128)
         kv[li, 0, :, 64:65].copy_(kh)
         kv[li, 1, :, 64:65].copy_(vh)
         att = torch.nn.functional.scaled_dot_product_attention(qh.unsqueeze(0), kv[li, 0].unsqueeze(0),
                                                                kv[li, 1].unsqueeze(0))
         h = h + lin(lw["o"], att.reshape(1, 512))
-        a = dec._rms(h, torch.ones(512, device="cuda", dtype=torch.float16))
+        a = _rms(h, torch.ones(512, device="cuda", dtype=torch.float16))
         m = torch.nn.functional.silu(lin(lw["gate"], a)) * lin(lw["up"], a)
         h = h + lin(lw["down"], m)
-    ref = lin(Wl, dec._rms(h, dec.norm)).reshape(-1).float()
+    ref = lin(Wl, _rms(h, dec.norm)).reshape(-1).float()
     err = float((logits - ref).abs().max() / ref.abs().max())
     assert err < 1e-2, err
     assert int(torch.argmax(logits)) == int(torch.argmax(ref))
