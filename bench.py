@@ -55,6 +55,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-llama", action="store_true", help="skip the 7B tensor-parallel decode step")
     ap.add_argument("--llama-steps", type=int, default=20)
+    ap.add_argument("--no-batched", action="store_true", help="skip the 70B-MLP batched-token config")
     return ap.parse_args()
 
 
@@ -368,6 +369,10 @@ def run_ecq(args):
                          f"symbols, {secs:.2f} s): oracle C restatement of interleaved_rans_decode per tile + "
                          f"dequant + matvec, {threads} threads over row slabs"}
 
+    batched = None
+    if not args.no_batched:
+        batched = run_batched(dev)
+
     llama = None
     if not args.no_llama:
         del step_graph, launch_graphs
@@ -404,6 +409,7 @@ def run_ecq(args):
         "e2e": e2e,
         "cpu_baseline": cpu,
         "llama7b_decode": llama,
+        "batched_70b_mlp": batched,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
@@ -412,6 +418,48 @@ def run_ecq(args):
     if world > 1:
         del step_graph, launch_graphs
         dist.destroy_process_group()
+
+
+def run_batched(dev):
+    """70B-MLP-shaped 28672 x 8192 matrix (Laplace b = 0.5, group-128 scales)
+    at token batches 1, 8, 32, 128: batch 1 runs the fused GEMV; larger batches
+    decode once to fp16 and multiply on the tensor cores. Returns tokens/s and
+    effective 4-bit GB/s per batch (CUDA events, 3 warm-up and 10 timed calls,
+    each timed call preceded by a 256 MB write that flushes L2)."""
+    import torch
+
+    import ecq_b200 as ecq
+    from ecq_b200 import synthetic as syn
+
+    M, K = 28672, 8192
+    g = torch.Generator(device=dev).manual_seed(0)
+    p = torch.tensor(syn.laplace_probs(LAPLACE_B), device=dev, dtype=torch.float32)
+    sym = torch.multinomial(p, M * K, replacement=True, generator=g).to(torch.uint8).reshape(M, K).cpu().numpy()
+    enc = ecq.encode_matrix(sym, group_size=GROUP)
+    m = ecq.DeviceMatrix.from_encoded(enc, group_size=GROUP, device=dev)
+    sc = torch.from_numpy(syn.group_scales(M, K, GROUP, seed=1)).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {"shape": [M, K], "bits_per_symbol": round(enc.bits_per_symbol, 4), "batches": {}}
+    for B in (1, 8, 32, 128):
+        x = torch.randn(B, K, device=dev, dtype=torch.float16, generator=g)
+        for _ in range(3):
+            m.matmul(x, sc)
+        times = []
+        for _ in range(10):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            m.matmul(x, sc)
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        ms = statistics.median(times)
+        out["batches"][str(B)] = {"ms": round(ms, 4), "tokens_per_s": round(B * 1000.0 / ms, 1),
+                                  "effective_4bit_gbs": round(M * K / 2 / (ms / 1e3) / 1e9, 1),
+                                  "path": "fused GEMV" if B <= 2 else "decode to fp16 + tensor-core GEMM"}
+    m.check()
+    return out
 
 
 def run_llama(args, world, rank, local, dev, barrier):

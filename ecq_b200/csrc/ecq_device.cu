@@ -158,7 +158,8 @@ struct MatrixParams {
     const __half* x;       // [cols]
     const __half* scales;  // [rows, ng]
     __half* y;             // [rows]
-    uint8_t* sym_out;      // [rows, cols] (decode mode)
+    uint8_t* sym_out;      // [rows, cols] (decode mode: symbols)
+    __half* w_out;         // [rows, cols] (decode mode: dequantised fp16 weights, when set)
     float* partials;       // [n_tiles, 8]
     uint32_t* slab_count;  // [n_slabs]
     uint32_t* status;
@@ -170,6 +171,10 @@ struct MatrixParams {
 };
 
 constexpr int kTileRows = 8;
+// what matrix_kernel does with the decoded symbols
+constexpr int kModeSymbols = 0;  // store uint8 symbols
+constexpr int kModeGemv = 1;     // fused dequant + GEMV
+constexpr int kModeWeights = 2;  // store dequantised fp16 weights
 // {-(2^23 + 8*2^14), -(2^23 + 8*2^14)} as f32x2
 constexpr uint64_t kNegBias2 = 0xCB020000CB020000ull;
 
@@ -339,7 +344,7 @@ __device__ __forceinline__ void finish_tile(const MatrixParams& p, uint32_t t, f
 
 // Decode one tile (buf = offset of its bytes in shared memory) and either
 // accumulate its GEMV contribution or store its symbols.
-template <int MPL, int GPL, bool GEMV, bool CONSTANT>
+template <int MPL, int GPL, int MODE, bool CONSTANT>
 __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, uint32_t buf, uint32_t tb,
                                              int lane, PendingSlab& pend) {
     constexpr int NSG = MPL / GPL;  // scale groups per tile row
@@ -355,9 +360,12 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
     a += 128;
     const uint32_t cent = ((p.flags >> ECQ_FLAG_CONSTANT_SYM_SHIFT) & 15u) << 14;  // constant table: sym field
 
+    constexpr bool GEMV = MODE == kModeGemv;
+    constexpr bool SCALED = MODE != kModeSymbols;  // needs the group scales
     float xs[MPL];  // x * 2^-14 (exact), this lane's columns of the tile
     float acc[kTileRows];
     float sc = 0.f;
+    if constexpr (MODE == kModeWeights) sc = load_row_scale<NSG, GPL>(p, r0, c0, lane) * 6.103515625e-05f;
     if constexpr (GEMV) {
 #pragma unroll
         for (int m = 0; m < MPL; ++m) {
@@ -375,8 +383,9 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
     for (int r = 0; r < rows_here; ++r) {
         float rowacc = 0.f;
         float sn = 0.f;
-        if constexpr (GEMV) {
+        if constexpr (SCALED) {
             if (r + 1 < rows_here) sn = load_row_scale<NSG, GPL>(p, r0 + r + 1, c0, lane);
+            if constexpr (MODE == kModeWeights) sn *= 6.103515625e-05f;  // scale * 2^-14
         }
 #pragma unroll
         for (int sg = 0; sg < NSG; ++sg) {
@@ -396,6 +405,9 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
                 unpack2(part2, lo, hi);
                 part = lo + hi;
             } else {
+                float gscale = 0.f;
+                if constexpr (MODE == kModeWeights) gscale = __shfl_sync(0xffffffffu, sc, sg);
+                (void)gscale;
 #pragma unroll
                 for (int mm = 0; mm < GPL; ++mm) {
                     const int m = sg * GPL + mm;
@@ -405,11 +417,14 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
                     } else {
                         e = decode_step(x, a, tb);
                     }
+                    const size_t idx = static_cast<size_t>(r0 + r) * p.cols + c0 + 32 * m + lane;
                     if constexpr (GEMV) {
                         part = fmaf(entry_weight(e), xs[m], part);
+                    } else if constexpr (MODE == kModeWeights) {
+                        // (sym - 8) * 2^14 exactly, times scale * 2^-14: one rounding to fp16
+                        p.w_out[idx] = __float2half_rn(entry_weight(e) * gscale);
                     } else {
-                        p.sym_out[static_cast<size_t>(r0 + r) * p.cols + c0 + 32 * m + lane] =
-                            static_cast<uint8_t>((e >> 14) & 15u);
+                        p.sym_out[idx] = static_cast<uint8_t>((e >> 14) & 15u);
                     }
                 }
             }
@@ -419,8 +434,8 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
 #pragma unroll
             for (int k = 0; k < kTileRows - 1; ++k) acc[k] = acc[k + 1];
             acc[kTileRows - 1] = rowacc;
-            sc = sn;
         }
+        if constexpr (SCALED) sc = sn;
     }
     if constexpr (!CONSTANT) {
         if (x != kL || (a - buf - lane) != len * 32u) atomicOr(p.status, ECQ_STATUS_CORRUPT);
@@ -439,8 +454,9 @@ __host__ __device__ constexpr uint32_t overrun_pad() {
     return (32u * (5u + 3u * kTileRows * MPL) + 127u) & ~127u;
 }
 
-template <int MPL, int GPL, bool GEMV>
+template <int MPL, int GPL, int MODE>
 __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
+    constexpr bool GEMV = MODE == kModeGemv;
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -512,9 +528,9 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
         uint32_t buf = sbase + my_buf0 + stage * p.buf_bytes;
         asm volatile("" : "+r"(buf)::"memory");  // keep this tile's byte loads after its wait
         if (constant)
-            process_tile<MPL, GPL, GEMV, true>(p, t, buf, sbase, lane, pend);
+            process_tile<MPL, GPL, MODE, true>(p, t, buf, sbase, lane, pend);
         else
-            process_tile<MPL, GPL, GEMV, false>(p, t, buf, sbase, lane, pend);
+            process_tile<MPL, GPL, MODE, false>(p, t, buf, sbase, lane, pend);
     }
     if constexpr (GEMV) complete_pending(p, pend, lane);
     // never leave a bulk copy in flight when exiting after a timeout
@@ -529,10 +545,10 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
 // ---------------------------------------------------------------------------
 using KernelFn = void (*)(MatrixParams);
 
-template <bool GEMV>
+template <int MODE>
 KernelFn pick_kernel(int mpl, int gpl) {
 #define ECQ_CASE(M_, G_) \
-    if (mpl == M_ && gpl == G_) return matrix_kernel<M_, G_, GEMV>;
+    if (mpl == M_ && gpl == G_) return matrix_kernel<M_, G_, MODE>;
     ECQ_CASE(4, 1) ECQ_CASE(4, 2) ECQ_CASE(4, 4)
     ECQ_CASE(8, 1) ECQ_CASE(8, 2) ECQ_CASE(8, 4) ECQ_CASE(8, 8)
     ECQ_CASE(16, 1) ECQ_CASE(16, 2) ECQ_CASE(16, 4) ECQ_CASE(16, 8) ECQ_CASE(16, 16)
@@ -572,7 +588,9 @@ struct LaunchShape {
     uint32_t x_bytes;
 };
 
-int32_t shape_for(const ecq_matrix_view* m, bool gemv, LaunchShape* ls) {
+// groups: the kernel applies group scales (GEMV or fp16 weights); stage_x: GEMV
+int32_t shape_for(const ecq_matrix_view* m, bool groups, bool stage_x, LaunchShape* ls) {
+    const bool gemv = groups;
     if (!m) return ECQ_ERR_ARG;
     if (m->tile_rows != kTileRows) return ECQ_ERR_UNSUPPORTED;
     if (m->tile_cols % 32 || m->tile_cols == 0 || m->cols % m->tile_cols) return ECQ_ERR_SHAPE;
@@ -588,7 +606,9 @@ int32_t shape_for(const ecq_matrix_view* m, bool gemv, LaunchShape* ls) {
             return ECQ_ERR_UNSUPPORTED;
         }
     }
-    if (!(gemv ? pick_kernel<true>(mpl, gpl) : pick_kernel<false>(mpl, gpl))) return ECQ_ERR_UNSUPPORTED;
+    if (!(stage_x ? pick_kernel<kModeGemv>(mpl, gpl)
+                  : (groups ? pick_kernel<kModeWeights>(mpl, gpl) : pick_kernel<kModeSymbols>(mpl, gpl))))
+        return ECQ_ERR_UNSUPPORTED;
     const uint32_t slabs = (m->rows + kTileRows - 1) / kTileRows;
     if (m->n_tiles != slabs * (m->cols / m->tile_cols)) return ECQ_ERR_SHAPE;
     uint32_t buf = (m->max_tile_bytes + 127u) & ~127u;
@@ -596,7 +616,7 @@ int32_t shape_for(const ecq_matrix_view* m, bool gemv, LaunchShape* ls) {
     const int bar_bytes = 8 * (2 * 32 + 1);
     const int pad = static_cast<int>((32u * (5u + 3u * kTileRows * static_cast<uint32_t>(mpl)) + 127u) & ~127u);
     // stage x in shared memory when it leaves room for at least 16 warps
-    uint32_t xb = gemv ? m->cols * 2u : 0u;
+    uint32_t xb = stage_x ? m->cols * 2u : 0u;
     if (xb > static_cast<uint32_t>(kMaxSmem - kTableBytes - pad - bar_bytes) - 16u * 2u * buf) xb = 0;
     const int xpad = static_cast<int>((xb + 127u) & ~127u);
     int warps = static_cast<int>((kMaxSmem - kTableBytes - xpad - pad - bar_bytes) / (2 * static_cast<int64_t>(buf)));
@@ -613,9 +633,10 @@ int32_t shape_for(const ecq_matrix_view* m, bool gemv, LaunchShape* ls) {
 }
 
 int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, const __half* scales, __half* y,
-                      uint8_t* sym_out, void* workspace, uint32_t* status, cudaStream_t stream) {
+                      uint8_t* sym_out, void* workspace, uint32_t* status, cudaStream_t stream,
+                      __half* w_out = nullptr) {
     LaunchShape ls;
-    int32_t rc = shape_for(m, gemv, &ls);
+    int32_t rc = shape_for(m, gemv || w_out != nullptr, gemv, &ls);
     if (rc != ECQ_OK) return rc;
     MatrixParams p{};
     p.data = m->data;
@@ -626,6 +647,7 @@ int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, cons
     p.scales = scales;
     p.y = y;
     p.sym_out = sym_out;
+    p.w_out = w_out;
     p.status = status;
     p.rows = m->rows;
     p.cols = m->cols;
@@ -642,7 +664,8 @@ int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, cons
         p.slab_count = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) +
                                                    static_cast<size_t>(m->n_tiles) * kTileRows * sizeof(float));
     }
-    KernelFn fn = gemv ? pick_kernel<true>(ls.mpl, ls.gpl) : pick_kernel<false>(ls.mpl, ls.gpl);
+    KernelFn fn = gemv ? pick_kernel<kModeGemv>(ls.mpl, ls.gpl)
+                       : (w_out ? pick_kernel<kModeWeights>(ls.mpl, ls.gpl) : pick_kernel<kModeSymbols>(ls.mpl, ls.gpl));
     if (!ensure_smem_limit(reinterpret_cast<const void*>(fn), kMaxSmem)) return ECQ_ERR_CUDA;
     fn<<<ls.ctas, ls.warps * 32, ls.smem, stream>>>(p);
     return cudaGetLastError() == cudaSuccess ? ECQ_OK : ECQ_ERR_CUDA;
@@ -677,6 +700,16 @@ int32_t ecq_matrix_decode(const ecq_matrix_view* m, uint8_t* d_out, uint32_t* d_
                          static_cast<cudaStream_t>(stream));
 }
 
+int32_t ecq_matrix_dequantize(const ecq_matrix_view* m, const void* scales_f16, void* w_out_f16, uint32_t* d_status,
+                              void* stream) {
+    if (!view_ok(m) || !scales_f16 || !w_out_f16 || !d_status) return ECQ_ERR_ARG;
+    if (m->group_size == 0 || m->group_size % 32 || (m->group_size < m->tile_cols && m->tile_cols % m->group_size) ||
+        (m->group_size >= m->tile_cols && m->group_size % m->tile_cols))
+        return ECQ_ERR_UNSUPPORTED;
+    return launch_matrix(m, false, nullptr, static_cast<const __half*>(scales_f16), nullptr, nullptr, nullptr,
+                         d_status, static_cast<cudaStream_t>(stream), static_cast<__half*>(w_out_f16));
+}
+
 int64_t ecq_gemv_workspace_bytes(const ecq_matrix_view* m, uint32_t batch) {
     (void)batch;
     if (!m || !m->rows || !m->n_tiles) return ECQ_ERR_ARG;
@@ -704,7 +737,7 @@ int32_t ecq_device_info(int32_t* sm_count, int32_t* gemv_ctas, int32_t* gemv_war
     if (sm_count) *sm_count = sm_count_cached();
     if (m) {
         LaunchShape ls;
-        int32_t rc = shape_for(m, true, &ls);
+        int32_t rc = shape_for(m, true, true, &ls);
         if (rc != ECQ_OK) return rc;
         if (gemv_ctas) *gemv_ctas = ls.ctas;
         if (gemv_warps_per_cta) *gemv_warps_per_cta = ls.warps;

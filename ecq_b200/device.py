@@ -95,6 +95,33 @@ class DeviceMatrix:
         check(lib().ecq_matrix_decode(v, ptr(out), ptr(self.status), _stream_ptr(stream)), "matrix decode")
         return out
 
+    def dequantize(self, scales: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Decode to dequantised fp16 weights [rows, cols] = (sym - 8) * scale."""
+        ng = (self.cols + self.group_size - 1) // self.group_size
+        if scales.dtype != torch.float16 or tuple(scales.shape) != (self.rows, ng):
+            raise ValueError(f"scales must be float16 [{self.rows}, {ng}]")
+        _require_cuda(scales, "scales")
+        if out is None:
+            out = torch.empty(self.rows, self.cols, dtype=torch.float16, device=self.device)
+        _require_cuda(out, "out")
+        check(lib().ecq_matrix_dequantize(self.view(), ptr(scales), ptr(out), ptr(self.status), _stream_ptr(stream)),
+              "matrix dequantize")
+        return out
+
+    def matmul(self, x: torch.Tensor, scales: torch.Tensor, fused_max_batch: int = 2) -> torch.Tensor:
+        """y = x @ W^T for x [..., cols] fp16. Up to `fused_max_batch` rows run
+        the fused GEMV per row; larger batches decode W once to fp16
+        (dequantize) and multiply on the tensor cores with fp32 accumulation,
+        so the decode cost is paid once for the whole batch."""
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, self.cols)
+        if x2.shape[0] <= fused_max_batch:
+            y = self.gemv(x2.contiguous(), scales)
+        else:
+            w = self.dequantize(scales)
+            y = torch.mm(x2, w.t(), out_dtype=torch.float32).to(torch.float16)
+        return y.reshape(*lead, self.rows)
+
     def gemv(self, x: torch.Tensor, scales: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
         """y[b] = W_deq x[b] (fp16 in/out, fp32 accumulation); x [B, cols] or [cols]."""
         squeeze = x.dim() == 1

@@ -146,6 +146,14 @@ int32_t ecq_decode_interleaved(const uint8_t *d_data, const uint32_t *d_lengths,
  * parallel_rans_decode_async, src/decode_strategies.py:336-390). */
 int32_t ecq_matrix_decode(const ecq_matrix_view *m, uint8_t *d_out, uint32_t *d_status, void *stream);
 
+/* Decode a packed matrix straight to dequantised fp16 weights
+ * w_out[r, c] = (sym[r,c] - 8) * scales[r, c/g] (row-major [rows, cols]):
+ * the batched-token path, which decodes once and hands W to a tensor-core
+ * GEMM. Replaces the reference's CACHED dequantisation
+ * (src/decode_strategies.py:43-73 then src/quantizer.py:33-35). */
+int32_t ecq_matrix_dequantize(const ecq_matrix_view *m, const void *scales_f16, void *w_out_f16, uint32_t *d_status,
+                              void *stream);
+
 /* ---------------- device: fused decode + dequant + GEMV ---------------- */
 
 /* Bytes of device workspace ecq_gemv needs for this matrix and batch. The

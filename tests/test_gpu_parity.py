@@ -171,3 +171,21 @@ def test_llama_shapes_full_size(M, K):
     m.check()
     y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), 128, x.astype(np.float32))
     assert _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL
+
+
+def test_dequantize_and_batched_matmul():
+    M, K, g = 520, 2048, 128
+    sym = syn.laplace_symbols(M, K, b=0.5, seed=12)
+    sc = syn.group_scales(M, K, g, seed=13)
+    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, group_size=g), group_size=g)
+    s = torch.from_numpy(sc).cuda()
+    w = m.dequantize(s)
+    m.check()
+    w_ref = ((sym.astype(np.float32) - 8.0) * np.repeat(sc.astype(np.float32), g, axis=1)).astype(np.float16)
+    assert np.array_equal(w.cpu().numpy(), w_ref)
+    for B in (1, 2, 3, 8, 32):
+        x = syn.activations(B, K, seed=14 + B)
+        y = m.matmul(torch.from_numpy(x).cuda(), s)
+        m.check()
+        y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), g, x.astype(np.float32))
+        assert y.shape == (B, M) and _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL, B
