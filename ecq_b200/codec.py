@@ -60,6 +60,19 @@ class RANSTable:
         return cls.from_freq(f, "clamped" if norm[0] else "reference")
 
     @classmethod
+    def from_counts_reference(cls, counts) -> "RANSTable":
+        """Exactly the reference normaliser (src/rans.py:39-60), including the
+        frequency-0 outcome for rare symbols. For reading reference files,
+        whose RANSTable.from_bytes re-runs it on the stored frequencies."""
+        c = np.maximum(np.asarray(counts, dtype=np.float64), 1.0)
+        f = (c / c.sum() * PROB_SCALE).astype(np.uint32)
+        f[np.argmax(f)] += np.uint32(PROB_SCALE - int(f.sum()))
+        cum = np.zeros(NSYM + 1, dtype=np.uint32)
+        cum[1:] = np.cumsum(f)
+        st = np.repeat(np.arange(NSYM, dtype=np.uint8), f.astype(np.int64))
+        return cls(freq=f, cumfreq=cum, sym_table=st, n_symbols=NSYM, normaliser="reference")
+
+    @classmethod
     def from_symbols(cls, symbols) -> "RANSTable":
         return cls.from_counts(np.bincount(np.asarray(symbols, dtype=np.uint8).reshape(-1), minlength=NSYM))
 

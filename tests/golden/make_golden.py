@@ -22,7 +22,13 @@ It imports the reference's own ``src/rans.py`` and ``src/interleaved_rans.py``
                   float64;
 * tiled.npz       a matrix cut into 8x256 tiles, each tile's row-major symbols
                   encoded with 32 interleaved streams (the packed format's tile
-                  encoding).
+                  encoding);
+* v1_two_tensors.ecq + v1.npz  a two-tensor ".ecq" v1 file written by the
+                  reference's ModelCompressor (src/compressed_format.py:109-259),
+                  what its ModelDecompressor returns for each tensor (the second
+                  raises: the writer's offsets assume interleaved table/data
+                  blocks but it writes all tables first), and the dequantised
+                  quantize_affine output for each tensor.
 
 Where the reference normaliser gives frequency 0 to a symbol that occurs (its
 encoder never terminates on such input), a clamped table (every frequency at
@@ -211,6 +217,36 @@ def main(ref_root: str) -> None:
             i += 1
     flat["n_tiles"] = np.array(i)
     np.savez_compressed(out / "tiled.npz", **flat)
+    # ---------------- .ecq v1 container written by the reference ----------------
+    from src.compressed_format import CompressedModel, ModelCompressor, ModelDecompressor  # type: ignore
+    from src.quantizer import quantize_affine  # type: ignore
+
+    mc = ModelCompressor()
+    rng = np.random.default_rng(5)
+    metas, tbs, dbs, off = {}, [], [], 0
+    expect = {}
+    for name, shape in (("a", (48, 64)), ("b", (32, 100))):
+        wv = (rng.standard_normal(shape) * 0.02).astype(np.float32)
+        meta, tb, db = mc.compress_tensor(name, wv)
+        meta.table_offset = off
+        off += len(tb)
+        meta.data_offset = off
+        off += len(db)
+        metas[name] = meta
+        tbs.append(tb)
+        dbs.append(db)
+        expect[f"{name}_dequant"] = quantize_affine(wv, bits=4).dequantize().astype(np.float32)
+    v1 = out / "v1_two_tensors.ecq"
+    mc._write_file(v1, CompressedModel(tensors=metas, data=b"".join(tbs) + b"".join(dbs)))
+    md = ModelDecompressor()
+    loaded = md.load(v1)
+    expect["a_reference"] = md.decompress_tensor(loaded, "a")
+    try:
+        md.decompress_tensor(loaded, "b")
+        expect["b_reference_raises"] = np.array(0)
+    except Exception:
+        expect["b_reference_raises"] = np.array(1)
+    np.savez_compressed(out / "v1.npz", **expect)
     print("golden vectors written to", out)
 
 

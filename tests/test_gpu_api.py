@@ -130,3 +130,26 @@ def test_smart_decoder_modes(mat):
             d.get_weights("absent")
     dq = strategies.DecodedWeights(torch.from_numpy(sym[:2]).cuda(), 0.5, -4.0, (2, m.cols)).dequantize()
     assert torch.allclose(dq.cpu(), torch.from_numpy(sym[:2].astype(np.float32) * 0.5 - 4.0))
+
+
+def test_containers_on_gpu(tmp_path):
+    from conftest import GOLDEN
+    from ecq_b200 import container
+
+    z = np.load(GOLDEN / "v1.npz")
+    ref = container.read_ecq_v1(GOLDEN / "v1_two_tensors.ecq", layout="reference")
+    assert np.array_equal(container.decompress_v1_tensor(ref["a"]), z["a_reference"])
+    aw = container.read_ecq_v1(GOLDEN / "v1_two_tensors.ecq", layout="as_written")
+    for name in ("a", "b"):
+        assert np.allclose(container.decompress_v1_tensor(aw[name]), z[f"{name}_dequant"], atol=1e-7)
+    # v2: write, memory-map, load to the device, fused GEMV
+    w = syn.student_t_weights(264, 1024, seed=8).astype(np.float32)
+    container.save_ecq2(tmp_path / "m.ecq", {"w": container.compress_weights(w, 128)})
+    t = container.load_ecq2(tmp_path / "m.ecq")["w"]
+    m, s = t.to_device()
+    x = syn.activations(1, 1024, seed=9)
+    y = m.gemv(torch.from_numpy(x).cuda(), s)
+    m.check()
+    sym, sc = syn.quantize_symmetric_groups(w, 128)
+    assert _rel(y.float().cpu().numpy(), oracle.dequant_gemv(sym, sc.astype(np.float32), 128,
+                                                             x.astype(np.float32))) <= RTOL
