@@ -56,6 +56,7 @@ def parse():
     ap.add_argument("--no-llama", action="store_true", help="skip the 7B tensor-parallel decode step")
     ap.add_argument("--llama-steps", type=int, default=20)
     ap.add_argument("--no-batched", action="store_true", help="skip the 70B-MLP batched-token config")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the 8192x8192 entropy sweep")
     return ap.parse_args()
 
 
@@ -371,7 +372,11 @@ def run_ecq(args):
 
     batched = None
     if not args.no_batched:
-        batched = run_batched(dev)
+        batched = run_batched(dev, world, rank, barrier)
+
+    sweep = None
+    if not args.no_sweep and world == 1:
+        sweep = run_entropy_sweep(dev)
 
     llama = None
     if not args.no_llama:
@@ -410,6 +415,7 @@ def run_ecq(args):
         "cpu_baseline": cpu,
         "llama7b_decode": llama,
         "batched_70b_mlp": batched,
+        "entropy_sweep_8192": sweep,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
@@ -420,46 +426,131 @@ def run_ecq(args):
         dist.destroy_process_group()
 
 
-def run_batched(dev):
+def _median_ms(fn, flush, reps=10, warm=3, barrier=None):
+    """Median CUDA-event time of fn() over `reps` calls, each preceded by a
+    write of `flush` (larger than L2) so that no call finds its inputs in L2."""
+    import torch
+
+    for _ in range(warm):
+        fn()
+    times = []
+    for _ in range(reps):
+        flush.zero_()
+        if barrier is not None:
+            barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    return statistics.median(times)
+
+
+def _device_laplace(M, K, b, dev, seed):
+    import torch
+
+    from ecq_b200 import synthetic as syn
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    p = torch.tensor(syn.laplace_probs(b), device=dev, dtype=torch.float32)
+    return torch.multinomial(p, M * K, replacement=True, generator=g).to(torch.uint8).reshape(M, K).cpu().numpy()
+
+
+def run_batched(dev, world=1, rank=0, barrier=None):
     """70B-MLP-shaped 28672 x 8192 matrix (Laplace b = 0.5, group-128 scales)
     at token batches 1, 8, 32, 128: batch 1 runs the fused GEMV; larger batches
-    decode once to fp16 and multiply on the tensor cores. Returns tokens/s and
-    effective 4-bit GB/s per batch (CUDA events, 3 warm-up and 10 timed calls,
-    each timed call preceded by a 256 MB write that flushes L2)."""
+    decode once to fp16 and multiply on the tensor cores. With several ranks
+    the matrix is column-sharded: each rank holds an even share of the K-tiles
+    (same encoding), computes a partial y and an NCCL all-reduce sums them.
+    Returns tokens/s and effective 4-bit GB/s per batch (CUDA events, max over
+    ranks; 3 warm-up and 10 timed calls, each preceded by a 256 MB write that
+    flushes L2)."""
+    import torch
+    import torch.distributed as dist
+
+    import ecq_b200 as ecq
+    from ecq_b200 import synthetic as syn
+    from ecq_b200.codec import slice_matrix, split_even
+
+    M, K = 28672, 8192
+    sym = _device_laplace(M, K, LAPLACE_B, dev, 0)
+    enc = ecq.encode_matrix(sym, group_size=GROUP)
+    sc_all = syn.group_scales(M, K, GROUP, seed=1)
+    nk = K // enc.tile_cols
+    kt0, kt1 = split_even(nk, world)[rank]
+    if world > 1:
+        enc = slice_matrix(enc, 0, (M + 7) // 8, kt0, kt1)
+    c0, c1 = kt0 * enc.tile_cols, kt1 * enc.tile_cols
+    m = ecq.DeviceMatrix.from_encoded(enc, group_size=GROUP, device=dev)
+    sc = torch.from_numpy(np.ascontiguousarray(sc_all[:, c0 // GROUP:c1 // GROUP])).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    gx = torch.Generator(device=dev).manual_seed(5)
+    out = {"shape": [M, K], "bits_per_symbol": round(enc.bits_per_symbol, 4), "n_gpus": world,
+           "shard": f"K-tiles [{kt0}, {kt1}) of {nk} per rank" if world > 1 else "whole matrix",
+           "batches": {}}
+    for B in (1, 8, 32, 128):
+        x = torch.randn(B, K, device=dev, dtype=torch.float16, generator=gx)[:, c0:c1].contiguous()
+
+        def call():
+            y = m.matmul(x, sc)
+            if world > 1:
+                dist.all_reduce(y)
+            return y
+
+        ms = _median_ms(call, flush, barrier=barrier)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        out["batches"][str(B)] = {"ms": round(ms, 4), "tokens_per_s": round(B * 1000.0 / ms, 1),
+                                  "effective_4bit_gbs": round(M * K / 2 / (ms / 1e3) / 1e9, 1),
+                                  "path": ("fused GEMV" if B <= 2 else "decode to fp16 + tensor-core GEMM")
+                                  + (" + NCCL all-reduce" if world > 1 else "")}
+    m.check()
+    return out
+
+
+def run_entropy_sweep(dev):
+    """8192 x 8192 at batch 1 over Laplace scales b in {0.3, 0.5, 1, 2, 100}
+    and group sizes 64 and 128: the fused GEMV's time against the compressed
+    size, mapping where decode (symbols/s) rather than HBM bytes bounds it.
+    Median of 10 CUDA-event timed calls, each after a 256 MB L2 flush."""
     import torch
 
     import ecq_b200 as ecq
     from ecq_b200 import synthetic as syn
 
-    M, K = 28672, 8192
-    g = torch.Generator(device=dev).manual_seed(0)
-    p = torch.tensor(syn.laplace_probs(LAPLACE_B), device=dev, dtype=torch.float32)
-    sym = torch.multinomial(p, M * K, replacement=True, generator=g).to(torch.uint8).reshape(M, K).cpu().numpy()
-    enc = ecq.encode_matrix(sym, group_size=GROUP)
-    m = ecq.DeviceMatrix.from_encoded(enc, group_size=GROUP, device=dev)
-    sc = torch.from_numpy(syn.group_scales(M, K, GROUP, seed=1)).to(dev)
+    M = K = 8192
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    out = {"shape": [M, K], "bits_per_symbol": round(enc.bits_per_symbol, 4), "batches": {}}
-    for B in (1, 8, 32, 128):
-        x = torch.randn(B, K, device=dev, dtype=torch.float16, generator=g)
-        for _ in range(3):
-            m.matmul(x, sc)
-        times = []
-        for _ in range(10):
-            flush.zero_()
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            a.record()
-            m.matmul(x, sc)
-            b.record()
-            b.synchronize()
-            times.append(a.elapsed_time(b))
-        ms = statistics.median(times)
-        out["batches"][str(B)] = {"ms": round(ms, 4), "tokens_per_s": round(B * 1000.0 / ms, 1),
-                                  "effective_4bit_gbs": round(M * K / 2 / (ms / 1e3) / 1e9, 1),
-                                  "path": "fused GEMV" if B <= 2 else "decode to fp16 + tensor-core GEMM"}
-    m.check()
-    return out
+    x = torch.from_numpy(syn.activations(1, K, seed=2)).to(dev)
+    y = torch.empty(1, M, dtype=torch.float16, device=dev)
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    rows = []
+    for i, b in enumerate((0.3, 0.5, 1.0, 2.0, 100.0)):
+        sym = _device_laplace(M, K, b, dev, 100 + i)
+        for g in (64, 128):
+            enc = ecq.encode_matrix(sym, group_size=g)
+            m = ecq.DeviceMatrix.from_encoded(enc, group_size=g, device=dev)
+            sc = torch.from_numpy(syn.group_scales(M, K, g, seed=1)).to(dev)
+            ms = _median_ms(lambda: m.gemv(x, sc, out=y), flush)
+            m.check()
+            comp = enc.compressed_bytes + 4 * (enc.n_tiles + 1) + 64 * enc.n_tiles + 4 * 16384 + 2 * M * (K // g) \
+                + 2 * K + 2 * M
+            rows.append({"laplace_b": b, "group_size": g, "entropy_bits": round(syn.entropy_bits(syn.laplace_probs(b)), 3),
+                         "bits_per_symbol": round(enc.bits_per_symbol, 4), "tile": f"8x{enc.tile_cols}",
+                         "us": round(ms * 1e3, 2), "effective_4bit_gbs": round(M * K / 2 / (ms / 1e3) / 1e9, 1),
+                         "compressed_gbs": round(comp / (ms / 1e3) / 1e9, 1),
+                         "hbm_frac": round(comp / (ms / 1e3) / 1e9 / hbm, 4),
+                         "symbols_per_s": round(M * K / (ms / 1e3), 1)})
+            del m
+    return {"shape": [M, K], "batch": 1, "cases": rows}
 
 
 def run_llama(args, world, rank, local, dev, barrier):

@@ -189,3 +189,28 @@ def test_dequantize_and_batched_matmul():
         m.check()
         y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), g, x.astype(np.float32))
         assert y.shape == (B, M) and _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL, B
+
+
+@pytest.mark.parametrize("b", [0.3, 0.5, 1.0, 2.0, 100.0])
+def test_entropy_sweep_8192(b):
+    """The 8192x8192 entropy-sweep matrices (Laplace b from 0.3 to near-uniform):
+    decode(encode(W)) == W and the fused GEMV at group 64 and 128 against the
+    oracle's fp32 dequant + matvec."""
+    M = K = 8192
+    g = torch.Generator(device="cuda").manual_seed(int(b * 10))
+    p = torch.tensor(syn.laplace_probs(b), device="cuda", dtype=torch.float32)
+    sym = torch.multinomial(p, M * K, replacement=True, generator=g).to(torch.uint8).reshape(M, K).cpu().numpy()
+    x = syn.activations(1, K, seed=2)
+    for gs in (64, 128):
+        enc = ecq.encode_matrix(sym, group_size=gs)
+        m = ecq.DeviceMatrix.from_encoded(enc, group_size=gs)
+        if gs == 64:
+            out = m.decode()
+            torch.cuda.synchronize()
+            assert np.array_equal(out.cpu().numpy(), sym)
+            del out
+        sc = syn.group_scales(M, K, gs, seed=1)
+        y = m.gemv(torch.from_numpy(x).cuda(), torch.from_numpy(sc).cuda())
+        m.check()
+        y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), gs, x.astype(np.float32))
+        assert _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL, gs
