@@ -459,14 +459,15 @@ def _device_laplace(M, K, b, dev, seed):
 
 
 def run_batched(dev, world=1, rank=0, barrier=None):
-    """70B-MLP-shaped 28672 x 8192 matrix (Laplace b = 0.5, group-128 scales)
-    at token batches 1, 8, 32, 128: batch 1 runs the fused GEMV; larger batches
-    decode once to fp16 and multiply on the tensor cores. With several ranks
-    the matrix is column-sharded: each rank holds an even share of the K-tiles
-    (same encoding), computes a partial y and an NCCL all-reduce sums them.
-    Returns tokens/s and effective 4-bit GB/s per batch (CUDA events, max over
-    ranks; 3 warm-up and 10 timed calls, each preceded by a 256 MB write that
-    flushes L2)."""
+    """70B-MLP-shaped 28672 x 8192 matrix (Laplace b = 0.5, group-128 scales,
+    8x256 tiles) at token batches 1, 8, 32, 128: batch 1 runs the fused GEMV,
+    larger batches the tcgen05 kernel that decodes each tile straight into the
+    tensor core's shared-memory operand (no decoded weight in HBM). As a
+    control, the same encoding decoded to fp16 in HBM + a cuBLAS GEMM. With
+    several ranks the matrix is column-sharded: each rank holds an even share
+    of the K-tiles (same encoding), computes a partial y and an NCCL
+    all-reduce sums them. CUDA events, max over ranks; 3 warm-up and 10 timed
+    calls, each preceded by a 256 MB write that flushes L2."""
     import torch
     import torch.distributed as dist
 
@@ -474,9 +475,9 @@ def run_batched(dev, world=1, rank=0, barrier=None):
     from ecq_b200 import synthetic as syn
     from ecq_b200.codec import slice_matrix, split_even
 
-    M, K = 28672, 8192
+    M, K, TC = 28672, 8192, 256
     sym = _device_laplace(M, K, LAPLACE_B, dev, 0)
-    enc = ecq.encode_matrix(sym, group_size=GROUP)
+    enc = ecq.encode_matrix(sym, tile_cols=TC, group_size=GROUP)
     sc_all = syn.group_scales(M, K, GROUP, seed=1)
     nk = K // enc.tile_cols
     kt0, kt1 = split_even(nk, world)[rank]
@@ -487,27 +488,42 @@ def run_batched(dev, world=1, rank=0, barrier=None):
     sc = torch.from_numpy(np.ascontiguousarray(sc_all[:, c0 // GROUP:c1 // GROUP])).to(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     gx = torch.Generator(device=dev).manual_seed(5)
-    out = {"shape": [M, K], "bits_per_symbol": round(enc.bits_per_symbol, 4), "n_gpus": world,
+    out = {"shape": [M, K], "tile": f"8x{TC}", "bits_per_symbol": round(enc.bits_per_symbol, 4), "n_gpus": world,
            "shard": f"K-tiles [{kt0}, {kt1}) of {nk} per rank" if world > 1 else "whole matrix",
            "batches": {}}
+
+    def timed(fn):
+        ms = _median_ms(fn, flush, barrier=barrier)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
     for B in (1, 8, 32, 128):
         x = torch.randn(B, K, device=dev, dtype=torch.float16, generator=gx)[:, c0:c1].contiguous()
 
-        def call():
+        def fused():
             y = m.matmul(x, sc)
             if world > 1:
                 dist.all_reduce(y)
             return y
 
-        ms = _median_ms(call, flush, barrier=barrier)
-        if world > 1:
-            t = torch.tensor([ms], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        out["batches"][str(B)] = {"ms": round(ms, 4), "tokens_per_s": round(B * 1000.0 / ms, 1),
-                                  "effective_4bit_gbs": round(M * K / 2 / (ms / 1e3) / 1e9, 1),
-                                  "path": ("fused GEMV" if B <= 2 else "decode to fp16 + tensor-core GEMM")
-                                  + (" + NCCL all-reduce" if world > 1 else "")}
+        def control():
+            y = torch.mm(x, m.dequantize(sc).t(), out_dtype=torch.float32).to(torch.float16)
+            if world > 1:
+                dist.all_reduce(y)
+            return y
+
+        ms = timed(fused)
+        row = {"ms": round(ms, 4), "tokens_per_s": round(B * 1000.0 / ms, 1),
+               "effective_4bit_gbs": round(M * K / 2 / (ms / 1e3) / 1e9, 1),
+               "path": ("fused GEMV" if B == 1 else "fused decode + tcgen05 MMA (x in TMEM, W tile in SMEM)")
+               + (" + NCCL all-reduce" if world > 1 else "")}
+        if B > 1:
+            cms = timed(control)
+            row["control_decode_fp16_cublas_ms"] = round(cms, 4)
+        out["batches"][str(B)] = row
     m.check()
     return out
 

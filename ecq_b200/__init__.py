@@ -25,7 +25,7 @@ def __getattr__(name):
                 "verify_interleaved_roundtrip"):
         from . import interleaved
         return getattr(interleaved, name)
-    if name in ("entropy_coded_matmul", "EntropyCodedLinear", "rans_gemv"):
+    if name in ("entropy_coded_matmul", "EntropyCodedLinear", "rans_gemv", "rans_matmul"):
         from . import ops
         return getattr(ops, name)
     if name in ("SmartDecoder", "DecodeMode", "DecodedWeights"):

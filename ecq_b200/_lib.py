@@ -46,6 +46,8 @@ EXPORTS = (
     "ecq_gemv_workspace_bytes",
     "ecq_gemv",
     "ecq_gemv_noalloc",
+    "ecq_matmul_workspace_bytes",
+    "ecq_matmul",
     "ecq_device_info",
     "ecq_add_rmsnorm_f16",
     "ecq_rope_kv_f16",
@@ -88,6 +90,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "ecq_gemv_workspace_bytes": (c_int64, [POINTER(MatrixView), c_uint32]),
         "ecq_gemv": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, c_int64, P, P]),
         "ecq_gemv_noalloc": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, P]),
+        "ecq_matmul_workspace_bytes": (c_int64, [POINTER(MatrixView), c_uint32]),
+        "ecq_matmul": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, c_int64, P, P]),
         "ecq_device_info": (c_int32, [P, P, P, POINTER(MatrixView)]),
         "ecq_add_rmsnorm_f16": (c_int32, [P, P, P, P, P, c_int32, c_int32, ctypes.c_float, P]),
         "ecq_rope_kv_f16": (c_int32, [P, P, P, P, P, P, P, c_int32, c_int32, c_int64, P]),

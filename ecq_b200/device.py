@@ -46,6 +46,7 @@ class DeviceMatrix:
     dec_table: torch.Tensor    # int32 (bit pattern of uint32)
     workspace: torch.Tensor    # uint8, zero-filled
     status: torch.Tensor       # int32 [1]
+    mm_workspace: torch.Tensor | None = None  # uint8, zero-filled (tensor-core path)
 
     @classmethod
     def from_encoded(cls, enc: EncodedMatrix, group_size: int = 128, device="cuda") -> "DeviceMatrix":
@@ -108,15 +109,49 @@ class DeviceMatrix:
               "matrix dequantize")
         return out
 
-    def matmul(self, x: torch.Tensor, scales: torch.Tensor, fused_max_batch: int = 2) -> torch.Tensor:
+    def tensor_core_ok(self) -> bool:
+        """True when the tile layout has a tcgen05 kernel (tile widths 128, 256)."""
+        return int(lib().ecq_matmul_workspace_bytes(self.view(), 1)) > 0
+
+    def matmul_tc(self, x: torch.Tensor, scales: torch.Tensor, out: torch.Tensor | None = None,
+                  stream=None) -> torch.Tensor:
+        """y = x @ W^T for x [B, cols] fp16 on the tcgen05 tensor cores, each
+        tile decoded straight into the MMA's shared-memory operand (no decoded
+        weight in memory); fp32 accumulation, fp16 y [B, rows]."""
+        x2 = x.reshape(-1, self.cols)
+        if x2.dtype != torch.float16:
+            raise ValueError("x must be float16")
+        _require_cuda(x2, "x")
+        _require_cuda(scales, "scales")
+        ng = (self.cols + self.group_size - 1) // self.group_size
+        if scales.dtype != torch.float16 or tuple(scales.shape) != (self.rows, ng):
+            raise ValueError(f"scales must be float16 [{self.rows}, {ng}]")
+        if not x2.is_contiguous() or x2.data_ptr() % 16:
+            x2 = x2.contiguous().clone()
+        B = x2.shape[0]
+        if out is None:
+            out = torch.empty(B, self.rows, dtype=torch.float16, device=self.device)
+        _require_cuda(out, "out")
+        v = self.view()
+        need = int(lib().ecq_matmul_workspace_bytes(v, B))
+        check(need, "matmul workspace size")
+        if self.mm_workspace is None or self.mm_workspace.numel() < need:
+            self.mm_workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        check(lib().ecq_matmul(v, ptr(x2), ptr(scales), ptr(out), B, ptr(self.mm_workspace),
+                               self.mm_workspace.numel(), ptr(self.status), _stream_ptr(stream)), "matmul")
+        return out
+
+    def matmul(self, x: torch.Tensor, scales: torch.Tensor, fused_max_batch: int = 1) -> torch.Tensor:
         """y = x @ W^T for x [..., cols] fp16. Up to `fused_max_batch` rows run
-        the fused GEMV per row; larger batches decode W once to fp16
-        (dequantize) and multiply on the tensor cores with fp32 accumulation,
-        so the decode cost is paid once for the whole batch."""
+        the fused GEMV per row. Larger batches run the tcgen05 kernel
+        (matmul_tc) when the tile layout has one (tile widths 128 and 256);
+        8x512 tiles decode W once to fp16 (dequantize) for a tensor-core GEMM."""
         lead = x.shape[:-1]
         x2 = x.reshape(-1, self.cols)
         if x2.shape[0] <= fused_max_batch:
             y = self.gemv(x2.contiguous(), scales)
+        elif self.tensor_core_ok():
+            y = self.matmul_tc(x2, scales)
         else:
             w = self.dequantize(scales)
             y = torch.mm(x2, w.t(), out_dtype=torch.float32).to(torch.float16)
@@ -147,8 +182,10 @@ class DeviceMatrix:
         s = int(self.status.item())
         if reset and s:
             self.status.zero_()
-            # a call that did not finish may leave slab counters set
+            # a call that did not finish may leave slab counters or partial sums set
             self.workspace.zero_()
+            if self.mm_workspace is not None:
+                self.mm_workspace.zero_()
         return s
 
     def check(self) -> None:

@@ -3,6 +3,8 @@
 * ``torch.ops.ecq.rans_gemv`` -- a custom op over libecq's ``ecq_gemv``
   (with a fake implementation for shape propagation), so the fused GEMV can
   sit inside torch programs and CUDA graphs.
+* ``torch.ops.ecq.rans_matmul`` -- the same over ``ecq_matmul``, the
+  batched-token kernel on the tcgen05 tensor cores.
 * ``entropy_coded_matmul`` -- the fused op with the argument list of the
   reference's MLX plan (docs/mlx_integration_plan.md:222-237).
 * ``EntropyCodedLinear`` -- an ``nn.Linear`` replacement built with
@@ -60,6 +62,47 @@ def rans_gemv(x: torch.Tensor, m: DeviceMatrix, scales: torch.Tensor) -> torch.T
     return y[0] if x.dim() == 1 else y
 
 
+@torch.library.custom_op("ecq::rans_matmul", mutates_args=("workspace", "status"))
+def rans_matmul_op(x: torch.Tensor, data: torch.Tensor, tile_offset: torch.Tensor, stream_len: torch.Tensor,
+                   dec_table: torch.Tensor, scales: torch.Tensor, workspace: torch.Tensor, status: torch.Tensor,
+                   rows: int, cols: int, tile_rows: int, tile_cols: int, group_size: int, flags: int,
+                   max_tile_bytes: int) -> torch.Tensor:
+    """y[B, rows] = x[B, cols] @ dequant(W)^T on the tensor cores (tile widths
+    128 and 256), fp16 in/out, fp32 accumulation. `workspace` holds at least
+    ecq_matmul_workspace_bytes(B) zero bytes."""
+    if not x.is_cuda:
+        raise RuntimeError("ecq::rans_matmul runs on CUDA tensors only")
+    x2 = x.reshape(-1, cols).contiguous()
+    y = torch.empty(x2.shape[0], rows, dtype=torch.float16, device=x.device)
+    v = _view(data, tile_offset, stream_len, dec_table, rows, cols, tile_rows, tile_cols, group_size, flags,
+              max_tile_bytes)
+    check(lib().ecq_matmul(v, x2.data_ptr(), scales.data_ptr(), y.data_ptr(), x2.shape[0], workspace.data_ptr(),
+                           workspace.numel(), status.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream),
+          "ecq::rans_matmul")
+    return y
+
+
+@rans_matmul_op.register_fake
+def _(x, data, tile_offset, stream_len, dec_table, scales, workspace, status, rows, cols, tile_rows, tile_cols,
+      group_size, flags, max_tile_bytes):
+    return x.new_empty((x.numel() // cols, rows), dtype=torch.float16)
+
+
+def rans_matmul(x: torch.Tensor, m: DeviceMatrix, scales: torch.Tensor) -> torch.Tensor:
+    """x [B, cols] fp16 -> y [B, rows]: the tcgen05 kernel when the matrix's
+    tile layout has one, else the fused GEMV per token row."""
+    x2 = x.reshape(-1, m.cols)
+    if x2.shape[0] < 2 or not m.tensor_core_ok():
+        return rans_gemv(x2.contiguous(), m, scales)
+    need = int(lib().ecq_matmul_workspace_bytes(m.view(), x2.shape[0]))
+    check(need, "matmul workspace size")
+    if m.mm_workspace is None or m.mm_workspace.numel() < need:
+        m.mm_workspace = torch.zeros(need, dtype=torch.uint8, device=m.device)
+    return torch.ops.ecq.rans_matmul(x2, m.data, m.tile_offset, m.stream_len, m.dec_table, scales, m.mm_workspace,
+                                     m.status, m.rows, m.cols, m.tile_rows, m.tile_cols, m.group_size, m.flags,
+                                     m.max_tile_bytes)
+
+
 def entropy_coded_matmul(x: torch.Tensor, compressed_w: DeviceMatrix, stream_offsets=None, freq_table=None,
                          cumfreq_table=None, sym_table=None, scales: torch.Tensor | None = None,
                          biases: torch.Tensor | None = None, transpose: bool = True, group_size: int = 64,
@@ -93,7 +136,7 @@ def entropy_coded_matmul(x: torch.Tensor, compressed_w: DeviceMatrix, stream_off
         raise ValueError("scales are required")
     lead = x.shape[:-1]
     x2 = x.reshape(-1, m.cols).to(torch.float16).contiguous()
-    y = rans_gemv(x2, m, scales)
+    y = rans_matmul(x2, m, scales)
     if biases is not None:
         ng = scales.shape[1]
         pad = ng * group_size - m.cols
@@ -156,10 +199,11 @@ class EntropyCodedLinear(torch.nn.Module):
         if self.decode_mode == "cached":
             y = x2 @ self._weight.t()
         else:
-            y = rans_gemv(x2.contiguous(), self.matrix, self.scales)
+            y = rans_matmul(x2.contiguous(), self.matrix, self.scales)
         if self.bias is not None:
             y = y + self.bias
         return y.reshape(*lead, self.out_features)
 
 
-__all__ = ["rans_gemv", "rans_gemv_op", "entropy_coded_matmul", "EntropyCodedLinear", "_lib"]
+__all__ = ["rans_gemv", "rans_gemv_op", "rans_matmul", "rans_matmul_op", "entropy_coded_matmul", "EntropyCodedLinear",
+           "_lib"]

@@ -198,6 +198,26 @@ int32_t ecq_gemv(const ecq_matrix_view *m, const void *x_f16, const void *scales
 int32_t ecq_gemv_noalloc(const ecq_matrix_view *m, const void *x_f16, const void *scales_f16, void *y_f16,
                          uint32_t batch, uint32_t *d_status, void *stream);
 
+/* ---------------- device: fused decode + dequant + tensor-core GEMM ---------------- */
+
+/* Bytes of device workspace ecq_matmul needs for this matrix and batch, or a
+ * negative error code when the matrix's layout has no tensor-core kernel
+ * (tile widths 128 and 256 do; 512 does not). Zero-fill it once before first
+ * use; ecq_matmul leaves it zeroed again on completion. */
+int64_t ecq_matmul_workspace_bytes(const ecq_matrix_view *m, uint32_t batch);
+
+/* y = x . W^T for a token batch: y[b, r] = sum_c (sym[r,c] - 8) * scales[r, c/g]
+ * * x[b, c] with W rounded once to fp16 and fp32 accumulation on the tcgen05
+ * tensor cores, b < batch (any batch; 128 tokens per launch). Layouts as for
+ * ecq_gemv; x must be 16-byte aligned. Each tile is decoded straight into
+ * the tensor core's shared-memory operand: no decoded weight is written to
+ * memory. Replaces the reference's batched kernel tiled_parallel_gemm
+ * (src/metal_interleaved.py:375-484) and the MLX-side entropy_coded_matmul
+ * for x with several rows (docs/mlx_integration_plan.md:222-237). Returns
+ * ECQ_ERR_UNSUPPORTED for layouts ecq_matmul_workspace_bytes rejects. */
+int32_t ecq_matmul(const ecq_matrix_view *m, const void *x_f16, const void *scales_f16, void *y_f16,
+                   uint32_t batch, void *workspace, int64_t workspace_bytes, uint32_t *d_status, void *stream);
+
 /* Number of SMs and the persistent grid the fused kernel uses (for tests
  * and the benchmark's launch accounting). */
 int32_t ecq_device_info(int32_t *sm_count, int32_t *gemv_ctas, int32_t *gemv_warps_per_cta,

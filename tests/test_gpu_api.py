@@ -153,3 +153,43 @@ def test_containers_on_gpu(tmp_path):
     sym, sc = syn.quantize_symmetric_groups(w, 128)
     assert _rel(y.float().cpu().numpy(), oracle.dequant_gemv(sym, sc.astype(np.float32), 128,
                                                              x.astype(np.float32))) <= RTOL
+
+
+def test_rans_matmul_op_tensor_cores_and_graph():
+    """ecq::rans_matmul (tcgen05 path, 8x256 tiles) against the oracle, then
+    captured in a CUDA graph: replays give the same bits (fixed-point sums)."""
+    M, K, g = 456, 2048, 128
+    sym = syn.laplace_symbols(M, K, b=0.5, seed=51)
+    sc = syn.group_scales(M, K, g, seed=52)
+    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, tile_cols=256, group_size=g), group_size=g)
+    assert m.tensor_core_ok()
+    x = torch.from_numpy(syn.activations(12, K, seed=53)).cuda()
+    s = torch.from_numpy(sc).cuda()
+    y0 = ecq.rans_matmul(x, m, s).clone()
+    m.check()
+    assert _rel(y0.float().cpu().numpy(), oracle.dequant_gemv(sym, sc.astype(np.float32), g,
+                                                              x.float().cpu().numpy())) <= RTOL
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        y = ecq.rans_matmul(x, m, s)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    m.check()
+    assert torch.equal(y, y0)
+
+
+def test_entropy_coded_linear_batched_tensor_cores():
+    torch.manual_seed(1)
+    lin = torch.nn.Linear(2048, 520, bias=False).cuda()
+    with torch.no_grad():
+        lin.weight.normal_(0, 0.02)
+    ecl = ecq.EntropyCodedLinear.from_linear(lin, group_size=128, tile_cols=256)
+    assert ecl.matrix.tensor_core_ok()
+    x = torch.randn(2, 7, 2048, device="cuda", dtype=torch.float16)
+    y = ecl(x)
+    ecl.matrix.check()
+    assert ecl.matrix.mm_workspace is not None  # the batched call ran on the tensor cores
+    sym, sc = syn.quantize_symmetric_groups(lin.weight.detach().float().cpu().numpy(), 128)
+    y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), 128, x.reshape(14, 2048).float().cpu().numpy())
+    assert y.shape == (2, 7, 520) and _rel(y.reshape(14, 520).float().cpu().numpy(), y_ref) <= RTOL
