@@ -518,6 +518,8 @@ def run_batched(dev, world=1, rank=0, barrier=None):
         ms = timed(fused)
         row = {"ms": round(ms, 4), "tokens_per_s": round(B * 1000.0 / ms, 1),
                "effective_4bit_gbs": round(M * K / 2 / (ms / 1e3) / 1e9, 1),
+               "symbols_per_s": round(M * K / (ms / 1e3), 1),
+               "useful_tflops": round(2.0 * B * M * K / (ms / 1e3) / 1e12, 2),
                "path": ("fused GEMV" if B == 1 else "fused decode + tcgen05 MMA (x in TMEM, W tile in SMEM)")
                + (" + NCCL all-reduce" if world > 1 else "")}
         if B > 1:
