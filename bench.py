@@ -573,51 +573,66 @@ def run_entropy_sweep(dev):
 
 def run_llama(args, world, rank, local, dev, barrier):
     """Synthetic Llama-7B batch-1 decode step, tensor-parallel over the ranks,
-    captured in one CUDA graph (NCCL all-reduces included). Returns its summary."""
+    captured in one CUDA graph. With several ranks the row-parallel layers'
+    all-reduces run fused into the GEMV and the next add + RMSNorm over NVLink
+    peer memory; the same weights are also timed with NCCL all-reduces
+    (`tokens_per_s_nccl`). Returns the summary."""
     import torch
     import torch.distributed as dist
 
     from ecq_b200.model import Llama7BDecoder
 
     t0 = time.perf_counter()
-    dec = Llama7BDecoder(tp=world, rank=rank, device=dev, group=None)
+    dec = Llama7BDecoder(tp=world, rank=rank, device=dev, group=None, exchange="peer")
     build_s = time.perf_counter() - t0
     tok = torch.tensor([1], device=dev)
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        for _ in range(2):
-            dec.step(tok)
-        s.synchronize()
+
+    def timed(use_peer):
+        dec.use_peer = use_peer
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                dec.step(tok)
+            s.synchronize()
+            dec.check()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                out = dec.step(tok)
+            for _ in range(3):
+                g.replay()
+            s.synchronize()
+        barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            a.record(s)
+            for _ in range(args.llama_steps):
+                g.replay()
+            b.record(s)
+        b.synchronize()
+        ms = a.elapsed_time(b) / args.llama_steps
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dec.check()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=s):
-            out = dec.step(tok)
-        for _ in range(3):
-            g.replay()
-        s.synchronize()
-    barrier()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(s):
-        a.record(s)
-        for _ in range(args.llama_steps):
-            g.replay()
-        b.record(s)
-    b.synchronize()
-    ms = a.elapsed_time(b) / args.llama_steps
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    dec.check()
+        nxt = int(out.item())
+        del g
+        return float(t.item()), nxt
+
+    ms, nxt = timed(True)
     res = {"tokens_per_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 3), "tp": world,
+           "exchange": "fused peer-memory all-reduce (GEMV push + add/RMSNorm sum)" if world > 1 else "none",
            "steps": args.llama_steps, "symbols_per_token_per_rank": dec.symbols,
-           "compressed_bytes_per_rank": dec.compressed_bytes, "build_s": round(build_s, 1),
-           "next_token": int(out.item()),
+           "compressed_bytes_per_rank": dec.compressed_bytes, "build_s": round(build_s, 1), "next_token": nxt,
            "config": "32 layers, hidden 4096, 32 heads x 128, MLP 11008, vocab 32000, 2048-token fp16 KV cache; "
                      "Student-t(4)*0.02 weights, group-128 symmetric 4-bit, rANS per matrix; batch 1; CUDA graph"}
-    del g
+    if world > 1:
+        ms_n, nxt_n = timed(False)
+        res["tokens_per_s_nccl"] = round(1000.0 / ms_n, 2)
+        res["ms_per_token_nccl"] = round(ms_n, 3)
+        res["next_token_nccl"] = nxt_n
+    dec.close()
     return res
 
 

@@ -31,6 +31,8 @@ FLAG_CONSTANT = 1
 TILE_ROWS = 8
 NOALLOC_SCRATCH_BYTES = 4 << 20
 TABLE_ENTRIES = 16384
+TP_MAX_RANKS = 8
+IPC_HANDLE_BYTES = 64
 
 # every function include/*.h declares
 EXPORTS = (
@@ -49,6 +51,14 @@ EXPORTS = (
     "ecq_matmul_workspace_bytes",
     "ecq_matmul",
     "ecq_device_info",
+    "ecq_comm_buffer_bytes",
+    "ecq_comm_alloc",
+    "ecq_comm_free",
+    "ecq_ipc_get_handle",
+    "ecq_ipc_open",
+    "ecq_ipc_close",
+    "ecq_gemv_tp",
+    "ecq_tp_add_rmsnorm_f16",
     "ecq_add_rmsnorm_f16",
     "ecq_rope_kv_f16",
     "ecq_silu_mul_f16",
@@ -69,6 +79,15 @@ class MatrixView(ctypes.Structure):
         ("max_tile_bytes", c_uint32), ("flags", c_uint32),
         ("data", c_void_p), ("tile_offset", c_void_p),
         ("stream_len", c_void_p), ("dec_table", c_void_p),
+    ]
+
+
+class TPComm(ctypes.Structure):
+    """Mirror of ``ecq_tp_comm`` (include/ecq_comm.h)."""
+
+    _fields_ = [
+        ("world", c_uint32), ("rank", c_uint32), ("n_max", c_uint32), ("reserved", c_uint32),
+        ("local", c_void_p), ("peers", c_void_p * TP_MAX_RANKS),
     ]
 
 
@@ -93,6 +112,14 @@ def _declare(L: ctypes.CDLL) -> None:
         "ecq_matmul_workspace_bytes": (c_int64, [POINTER(MatrixView), c_uint32]),
         "ecq_matmul": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, c_int64, P, P]),
         "ecq_device_info": (c_int32, [P, P, P, POINTER(MatrixView)]),
+        "ecq_comm_buffer_bytes": (c_int64, [c_uint32, c_uint32]),
+        "ecq_comm_alloc": (c_int32, [c_int64, POINTER(c_void_p)]),
+        "ecq_comm_free": (c_int32, [P]),
+        "ecq_ipc_get_handle": (c_int32, [P, P]),
+        "ecq_ipc_open": (c_int32, [P, POINTER(c_void_p)]),
+        "ecq_ipc_close": (c_int32, [P]),
+        "ecq_gemv_tp": (c_int32, [POINTER(MatrixView), P, P, POINTER(TPComm), P, c_int64, P, P]),
+        "ecq_tp_add_rmsnorm_f16": (c_int32, [P, POINTER(TPComm), P, P, P, c_int32, ctypes.c_float, P, P]),
         "ecq_add_rmsnorm_f16": (c_int32, [P, P, P, P, P, c_int32, c_int32, ctypes.c_float, P]),
         "ecq_rope_kv_f16": (c_int32, [P, P, P, P, P, P, P, c_int32, c_int32, c_int64, P]),
         "ecq_silu_mul_f16": (c_int32, [P, P, c_int32, c_int32, P]),
@@ -137,4 +164,4 @@ def ptr(a) -> int:
     return a.ctypes.data
 
 
-__all__ = ["lib", "check", "ptr", "MatrixView", "EcqError", "EXPORTS", "c_uint16"]
+__all__ = ["lib", "check", "ptr", "MatrixView", "TPComm", "EcqError", "EXPORTS", "c_uint16"]

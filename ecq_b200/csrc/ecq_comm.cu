@@ -1,0 +1,154 @@
+// ecq_comm.cu -- the tensor-parallel exchange's host plumbing (exchange
+// buffers, CUDA IPC) and its consumer kernel. The producer side is the fused
+// GEMV's TP mode (ecq_gemv_tp, ecq_device.cu). Layout and protocol:
+// include/ecq_comm.h.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "ecq_comm.h"
+
+namespace {
+
+constexpr uint64_t kFlagWaitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* addr) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    return v;
+}
+
+// One CTA: wait for every rank's partials of this rank's epoch, sum them in
+// rank order, then h_out = h + d and y = rmsnorm(h_out) * w (the arithmetic
+// of ecq_add_rmsnorm_f16), and advance the epoch.
+__global__ void tp_add_rmsnorm_kernel(const __half* h, ecq_tp_comm c, const __half* __restrict__ w,
+                                      __half* h_out, __half* __restrict__ y, int n, float eps,
+                                      uint32_t* __restrict__ status) {
+    extern __shared__ float buf[];  // n floats + 32 partials
+    __shared__ uint32_t s_epoch;
+    uint32_t* epoch = static_cast<uint32_t*>(c.local);
+    if (threadIdx.x == 0) {
+        const uint32_t e = *reinterpret_cast<volatile uint32_t*>(epoch);
+        s_epoch = e;
+        const uint32_t* flags = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(c.local) + 128u) +
+                                (e & 1u) * ECQ_TP_MAX_RANKS;
+        const uint64_t t0 = global_timer_ns();
+        bool timed_out = false;
+        for (uint32_t r = 0; r < c.world && !timed_out; ++r) {
+            while (ld_acquire_sys_u32(flags + r) != e + 1u) {
+                if (global_timer_ns() - t0 > kFlagWaitNs) {
+                    atomicOr(status, ECQ_STATUS_TIMEOUT);
+                    timed_out = true;
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t e = s_epoch;
+    const float* part = reinterpret_cast<const float*>(static_cast<const uint8_t*>(c.local) + 256u) +
+                        static_cast<size_t>(e & 1u) * c.world * c.n_max;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float d = 0.f;
+        for (uint32_t r = 0; r < c.world; ++r) d += __ldcg(part + static_cast<size_t>(r) * c.n_max + i);
+        const float v = __half2float(__float2half_rn(__half2float(h[i]) + __half2float(__float2half_rn(d))));
+        buf[i] = v;
+        ss += v * v;
+    }
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    float* red = buf + n;
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) red[0] = rsqrtf(v / n + eps);
+    }
+    __syncthreads();
+    const float rs = red[0];
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = buf[i];
+        h_out[i] = __float2half_rn(v);
+        y[i] = __hmul(__float2half_rn(v * rs), w[i]);
+    }
+    __syncthreads();  // every partial has been read
+    if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(epoch) = e + 1u;
+}
+
+bool comm_ok(const ecq_tp_comm* c) {
+    if (!c || c->world < 1 || c->world > ECQ_TP_MAX_RANKS || c->rank >= c->world || !c->local) return false;
+    for (uint32_t q = 0; q < c->world; ++q)
+        if (!c->peers[q]) return false;
+    return c->peers[c->rank] == c->local;
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == ECQ_IPC_HANDLE_BYTES, "CUDA IPC handle size");
+
+}  // namespace
+
+extern "C" {
+
+int64_t ecq_comm_buffer_bytes(uint32_t n_max, uint32_t world) {
+    if (n_max == 0 || world < 1 || world > ECQ_TP_MAX_RANKS) return ECQ_ERR_ARG;
+    return 256 + 2ll * world * n_max * static_cast<int64_t>(sizeof(float));
+}
+
+int32_t ecq_comm_alloc(int64_t bytes, void** d_buf) {
+    if (!d_buf || bytes <= 0) return ECQ_ERR_ARG;
+    *d_buf = nullptr;
+    if (cudaMalloc(d_buf, static_cast<size_t>(bytes)) != cudaSuccess) return ECQ_ERR_CUDA;
+    if (cudaMemset(*d_buf, 0, static_cast<size_t>(bytes)) != cudaSuccess) {
+        cudaFree(*d_buf);
+        *d_buf = nullptr;
+        return ECQ_ERR_CUDA;
+    }
+    return ECQ_OK;
+}
+
+int32_t ecq_comm_free(void* d_buf) {
+    if (!d_buf) return ECQ_ERR_ARG;
+    return cudaFree(d_buf) == cudaSuccess ? ECQ_OK : ECQ_ERR_CUDA;
+}
+
+int32_t ecq_ipc_get_handle(const void* d_buf, void* handle_out) {
+    if (!d_buf || !handle_out) return ECQ_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, const_cast<void*>(d_buf)) != cudaSuccess) return ECQ_ERR_CUDA;
+    memcpy(handle_out, &h, sizeof(h));
+    return ECQ_OK;
+}
+
+int32_t ecq_ipc_open(const void* handle, void** d_mapped) {
+    if (!handle || !d_mapped) return ECQ_ERR_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    *d_mapped = nullptr;
+    if (cudaIpcOpenMemHandle(d_mapped, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return ECQ_ERR_CUDA;
+    return ECQ_OK;
+}
+
+int32_t ecq_ipc_close(void* d_mapped) {
+    if (!d_mapped) return ECQ_ERR_ARG;
+    return cudaIpcCloseMemHandle(d_mapped) == cudaSuccess ? ECQ_OK : ECQ_ERR_CUDA;
+}
+
+int32_t ecq_tp_add_rmsnorm_f16(const void* h, const ecq_tp_comm* comm, const void* w, void* h_out, void* y, int32_t n,
+                               float eps, uint32_t* d_status, void* stream) {
+    if (!h || !w || !h_out || !y || !d_status || !comm_ok(comm) || n < 1 || n > 12256 ||
+        static_cast<uint32_t>(n) > comm->n_max)
+        return ECQ_ERR_ARG;
+    const int threads = n >= 1024 ? 1024 : ((n + 31) / 32) * 32;
+    tp_add_rmsnorm_kernel<<<1, threads, (n + 32) * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const __half*>(h), *comm, static_cast<const __half*>(w), static_cast<__half*>(h_out),
+        static_cast<__half*>(y), n, eps, d_status);
+    return cudaGetLastError() == cudaSuccess ? ECQ_OK : ECQ_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -28,6 +28,7 @@
 // intact streams the two decoders are therefore identical.
 #include <algorithm>
 
+#include "ecq_comm.h"
 #include "ecq_kernels.cuh"
 
 namespace {
@@ -100,6 +101,12 @@ struct MatrixParams {
     uint32_t buf_bytes;
     uint32_t flags;
     uint32_t x_bytes;  // x staged in shared memory after the table (0: read x from global)
+    // tensor-parallel push (ecq_gemv_tp; tp_world == 0 otherwise): y goes as
+    // fp32 partials to every rank's exchange buffer instead of to p.y
+    uint8_t* tp_peer[ECQ_TP_MAX_RANKS];
+    uint32_t* tp_epoch;  // this rank's epoch counter
+    uint32_t* tp_done;   // row slabs finished in this launch (workspace)
+    uint32_t tp_world, tp_rank, tp_nmax, n_slabs;
 };
 
 // what matrix_kernel does with the decoded symbols
@@ -157,6 +164,39 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* addr, uint32_t v)
     return old;
 }
 
+// Tensor-parallel push of one finished row slab: its fp32 row sums go to
+// partials[e & 1][rank][row] of every rank's exchange buffer (plain stores,
+// through CUDA IPC mappings for the peers), fenced at system scope; the warp
+// that finishes the launch's last slab then raises flags[e & 1][rank] = e + 1
+// on every rank with a system-scope release. Buffer layout: include/ecq_comm.h.
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* addr, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t* addr, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void tp_push_slab(const MatrixParams& p, uint32_t slab, int row, bool writer, float s,
+                                             int lane) {
+    const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(p.tp_epoch);
+    if (writer) {
+        const size_t off = 256u + ((static_cast<size_t>(e & 1u) * p.tp_world + p.tp_rank) * p.tp_nmax +
+                                   static_cast<size_t>(slab) * kTileRows + row) * sizeof(float);
+        for (uint32_t q = 0; q < p.tp_world; ++q) *reinterpret_cast<float*>(p.tp_peer[q] + off) = s;
+    }
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) {
+        if (atom_add_acq_rel_sys(p.tp_done, 1u) == p.n_slabs - 1) {
+            *p.tp_done = 0u;  // read again by the next launch only
+            for (uint32_t q = 0; q < p.tp_world; ++q)
+                st_release_sys_u32(reinterpret_cast<uint32_t*>(p.tp_peer[q] + 128u) + (e & 1u) * ECQ_TP_MAX_RANKS + p.tp_rank,
+                                   e + 1u);
+        }
+    }
+}
+
 __device__ __forceinline__ void complete_pending(const MatrixParams& p, PendingSlab& pend, int lane) {
     if (pend.slab == 0xffffffffu) return;
     const uint32_t old = __shfl_sync(0xffffffffu, pend.old, 0);
@@ -169,7 +209,11 @@ __device__ __forceinline__ void complete_pending(const MatrixParams& p, PendingS
         for (uint32_t k = kp; k < p.n_ktiles; k += 4) s += __ldcg(base + static_cast<size_t>(k) * kTileRows + row);
         s += __shfl_xor_sync(0xffffffffu, s, 8);
         s += __shfl_xor_sync(0xffffffffu, s, 16);
-        if (kp == 0 && row < pend.rows) p.y[slab * kTileRows + row] = __float2half_rn(s);
+        if (p.tp_world == 0) {
+            if (kp == 0 && row < pend.rows) p.y[slab * kTileRows + row] = __float2half_rn(s);
+        } else {
+            tp_push_slab(p, slab, row, kp == 0 && row < pend.rows, s, lane);
+        }
         if (lane == 0) p.slab_count[slab] = 0u;
     }
     pend.slab = 0xffffffffu;
@@ -464,7 +508,7 @@ int32_t shape_for(const ecq_matrix_view* m, bool groups, bool stage_x, LaunchSha
 
 int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, const __half* scales, __half* y,
                       uint8_t* sym_out, void* workspace, uint32_t* status, cudaStream_t stream,
-                      __half* w_out = nullptr) {
+                      __half* w_out = nullptr, const ecq_tp_comm* comm = nullptr) {
     LaunchShape ls;
     int32_t rc = shape_for(m, gemv || w_out != nullptr, gemv, &ls);
     if (rc != ECQ_OK) return rc;
@@ -489,10 +533,19 @@ int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, cons
     p.flags = m->flags;
     // x staged by bulk copy needs a 16-byte aligned address
     p.x_bytes = (gemv && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) ? ls.x_bytes : 0u;
+    p.n_slabs = (m->rows + kTileRows - 1) / kTileRows;
     if (gemv) {
         p.partials = static_cast<float*>(workspace);
         p.slab_count = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) +
                                                    static_cast<size_t>(m->n_tiles) * kTileRows * sizeof(float));
+        p.tp_done = p.slab_count + p.n_slabs;
+    }
+    if (comm) {
+        p.tp_world = comm->world;
+        p.tp_rank = comm->rank;
+        p.tp_nmax = comm->n_max;
+        p.tp_epoch = static_cast<uint32_t*>(comm->local);
+        for (uint32_t q = 0; q < comm->world; ++q) p.tp_peer[q] = static_cast<uint8_t*>(comm->peers[q]);
     }
     KernelFn fn = gemv ? pick_kernel<kModeGemv>(ls.mpl, ls.gpl)
                        : (w_out ? pick_kernel<kModeWeights>(ls.mpl, ls.gpl) : pick_kernel<kModeSymbols>(ls.mpl, ls.gpl));
@@ -544,7 +597,8 @@ int64_t ecq_gemv_workspace_bytes(const ecq_matrix_view* m, uint32_t batch) {
     (void)batch;
     if (!m || !m->rows || !m->n_tiles) return ECQ_ERR_ARG;
     const int64_t slabs = (m->rows + kTileRows - 1) / kTileRows;
-    return static_cast<int64_t>(m->n_tiles) * kTileRows * 4 + slabs * 4;
+    // per-tile row partials, per-slab counters, one launch-wide slab counter (padded)
+    return static_cast<int64_t>(m->n_tiles) * kTileRows * 4 + slabs * 4 + 16;
 }
 
 int32_t ecq_gemv(const ecq_matrix_view* m, const void* x_f16, const void* scales_f16, void* y_f16, uint32_t batch,
@@ -560,6 +614,19 @@ int32_t ecq_gemv(const ecq_matrix_view* m, const void* x_f16, const void* scales
         if (rc != ECQ_OK) return rc;
     }
     return ECQ_OK;
+}
+
+int32_t ecq_gemv_tp(const ecq_matrix_view* m, const void* x_f16, const void* scales_f16, const ecq_tp_comm* comm,
+                    void* workspace, int64_t workspace_bytes, uint32_t* d_status, void* stream) {
+    if (!view_ok(m) || !x_f16 || !scales_f16 || !comm || !d_status) return ECQ_ERR_ARG;
+    if (comm->world < 1 || comm->world > ECQ_TP_MAX_RANKS || comm->rank >= comm->world || !comm->local ||
+        m->rows > comm->n_max)
+        return ECQ_ERR_ARG;
+    for (uint32_t q = 0; q < comm->world; ++q)
+        if (!comm->peers[q]) return ECQ_ERR_ARG;
+    if (!workspace || workspace_bytes < ecq_gemv_workspace_bytes(m, 1)) return ECQ_ERR_WORKSPACE;
+    return launch_matrix(m, true, static_cast<const __half*>(x_f16), static_cast<const __half*>(scales_f16), nullptr,
+                         nullptr, workspace, d_status, static_cast<cudaStream_t>(stream), nullptr, comm);
 }
 
 int32_t ecq_device_info(int32_t* sm_count, int32_t* gemv_ctas, int32_t* gemv_warps_per_cta,

@@ -105,10 +105,16 @@ class Llama7BDecoder:
     rank of a tensor-parallel group (tp = world size, rank = this rank)."""
 
     def __init__(self, cfg: Llama7BConfig | None = None, device=None, tp: int = 1, rank: int = 0, seed: int = 3,
-                 group=None):
+                 group=None, exchange: str = "peer"):
+        """exchange (tp > 1): "peer" fuses each row-parallel layer's all-reduce
+        into its GEMV and the next add + RMSNorm over NVLink peer memory
+        (ecq_b200.comm); "nccl" runs GEMV -> NCCL all-reduce -> add + RMSNorm."""
         self.cfg = cfg = cfg or Llama7BConfig()
         self.dev = torch.device(device or "cuda")
         self.tp, self.rank, self.group = tp, rank, group
+        if exchange not in ("peer", "nccl"):
+            raise ValueError("exchange is 'peer' or 'nccl'")
+        self.exchange = exchange if tp > 1 else "none"
         H, D = cfg.hidden, cfg.head_dim
         if cfg.heads % tp:
             raise ValueError("heads must divide evenly over the TP ranks")
@@ -174,6 +180,12 @@ class Llama7BDecoder:
         self.sin = torch.sin(ang).to(torch.float16)
         self.vocab_sizes = [min(hi * 8, cfg.vocab) - lo * 8 for lo, hi in split_even((cfg.vocab + 7) // 8, tp)]
         self.logits = torch.empty(tp, max(self.vocab_sizes), device=self.dev, dtype=torch.float16)
+        self.xch = None
+        self.use_peer = True  # with an exchange: False runs the NCCL path instead (same weights)
+        if self.exchange == "peer":
+            from .comm import PeerExchange
+
+            self.xch = PeerExchange(n_max=H, group=group, device=self.dev)
 
     # -- glue ------------------------------------------------------------------
     def _add_rms(self, h: torch.Tensor, d: torch.Tensor | None, w: torch.Tensor) -> torch.Tensor:
@@ -202,8 +214,10 @@ class Llama7BDecoder:
         stream = torch.cuda.current_stream(self.dev).cuda_stream
         h = self.embed[token].reshape(1, cfg.hidden).clone()
         d = None
+        peer = self.xch is not None and self.use_peer
+        pending = False  # the residual delta sits in the peer exchange (not in d)
         for li, lw in enumerate(self.layers):
-            a = self._add_rms(h, d, lw["ln1"])
+            a = self.xch.add_rmsnorm(h, lw["ln1"], cfg.eps) if pending else self._add_rms(h, d, lw["ln1"])
             qkv = lw["qkv"](a)                      # [1, 3L]: q | k | v
             kslot = self.kv[li, 0, :, cfg.kv_len]
             vslot = self.kv[li, 1, :, cfg.kv_len]
@@ -213,13 +227,21 @@ class Llama7BDecoder:
             q = qkv[:, :L].reshape(1, nh, 1, D)
             att = torch.nn.functional.scaled_dot_product_attention(q, self.kv[li, 0].unsqueeze(0),
                                                                    self.kv[li, 1].unsqueeze(0))
-            o = self._all_reduce(lw["o"](att.reshape(1, L)))
-            a = self._add_rms(h, o, lw["ln2"])
+            if peer:
+                self.xch.gemv_push(lw["o"].m, att.reshape(1, L).contiguous(), lw["o"].scales)
+                a = self.xch.add_rmsnorm(h, lw["ln2"], cfg.eps)
+            else:
+                o = self._all_reduce(lw["o"](att.reshape(1, L)))
+                a = self._add_rms(h, o, lw["ln2"])
             gu = lw["gate_up"](a)                   # [1, 2F]: gate | up
             m = torch.empty(1, F, device=self.dev, dtype=torch.float16)
             check(lib().ecq_silu_mul_f16(gu.data_ptr(), m.data_ptr(), F, 1, stream), "silu_mul")
-            d = self._all_reduce(lw["down"](m))
-        a = self._add_rms(h, d, self.norm)
+            if peer:
+                self.xch.gemv_push(lw["down"].m, m, lw["down"].scales)
+                pending = True
+            else:
+                d = self._all_reduce(lw["down"](m))
+        a = self.xch.add_rmsnorm(h, self.norm, cfg.eps) if pending else self._add_rms(h, d, self.norm)
         logits = self.lm_head(a).reshape(-1)
         if self.tp > 1:
             local = torch.full((self.logits.shape[1],), -65504.0, device=self.dev, dtype=torch.float16)
@@ -233,6 +255,14 @@ class Llama7BDecoder:
             for k in ("qkv", "o", "gate_up", "down"):
                 lw[k].m.check()
         self.lm_head.m.check()
+        if self.xch is not None:
+            self.xch.check()
+
+    def close(self) -> None:
+        """Release the peer exchange (collective over the TP group)."""
+        if self.xch is not None:
+            self.xch.close()
+            self.xch = None
 
 
 def tp_partition(cfg: Llama7BConfig, tp: int) -> list[dict]:

@@ -1,0 +1,126 @@
+"""The tensor-parallel exchange over NVLink peer memory (ecq_gemv_tp ->
+ecq_tp_add_rmsnorm_f16), on 2 GPUs: two spawned ranks, NCCL for the handle
+exchange and the comparison path. Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rel(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def _worker(rank, world, port, which):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        if which == "exchange":
+            _exchange(rank, world, dev)
+        else:
+            _decoder(rank, world, dev)
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[rank])
+        dist.destroy_process_group()
+
+
+def _exchange(rank, world, dev):
+    import ecq_b200 as ecq
+    from ecq_b200 import synthetic as syn
+    from ecq_b200.codec import slice_matrix, split_even
+    from ecq_b200.comm import PeerExchange
+    from oracle import oracle
+
+    M, K, g = 520, 2048, 128
+    sym = syn.laplace_symbols(M, K, b=0.5, seed=61)
+    sc = syn.group_scales(M, K, g, seed=62)
+    enc = ecq.encode_matrix(sym, tile_cols=512, group_size=g)
+    kt0, kt1 = split_even(K // 512, world)[rank]
+    m = ecq.DeviceMatrix.from_encoded(slice_matrix(enc, 0, (M + 7) // 8, kt0, kt1), group_size=g, device=dev)
+    c0, c1 = kt0 * 512, kt1 * 512
+    s_loc = torch.from_numpy(np.ascontiguousarray(sc[:, c0 // g:c1 // g])).to(dev)
+    w = torch.from_numpy((1.0 + 0.1 * np.random.default_rng(63).standard_normal(M)).astype(np.float16)).to(dev)
+    xch = PeerExchange(n_max=1024, device=dev)
+    try:
+        for it in range(5):  # several epochs: both buffer halves, flags re-armed
+            x = syn.activations(1, K, seed=70 + it)
+            h0 = syn.activations(1, M, seed=80 + it)
+            h = torch.from_numpy(h0).to(dev).reshape(-1).clone()
+            xch.gemv_push(m, torch.from_numpy(np.ascontiguousarray(x[0, c0:c1])).to(dev), s_loc)
+            y = xch.add_rmsnorm(h, w, 1e-5)
+            torch.cuda.synchronize()
+            m.check()
+            xch.check()
+            d = oracle.dequant_gemv(sym, sc.astype(np.float32), g, x.astype(np.float32))[0]
+            h_ref = (h0[0].astype(np.float32) + d.astype(np.float16).astype(np.float32)).astype(np.float16)
+            assert _rel(h.cpu().numpy(), h_ref) <= 2e-3, it
+            hf = h_ref.astype(np.float32)
+            y_ref = (hf / np.sqrt(np.mean(hf * hf) + 1e-5)).astype(np.float16).astype(np.float32) * \
+                w.float().cpu().numpy()
+            assert _rel(y.float().cpu().numpy(), y_ref) <= 2e-3, it
+    finally:
+        xch.close()
+
+
+def _decoder(rank, world, dev):
+    from ecq_b200.model import Llama7BConfig, Llama7BDecoder
+
+    cfg = Llama7BConfig(layers=2, hidden=512, heads=4, head_dim=128, mlp=1024, vocab=1000, kv_len=64)
+    tok = torch.tensor([17], device=dev)
+    ref = Llama7BDecoder(cfg, device=dev, tp=1, seed=5)
+    l_ref = ref.step_logits(tok).float()
+    dec = Llama7BDecoder(cfg, device=dev, tp=world, rank=rank, seed=5, exchange="peer")
+    try:
+        l_peer = dec.step_logits(tok).float()
+        dec.use_peer = False
+        l_nccl = dec.step_logits(tok).float()
+        dec.use_peer = True
+        torch.cuda.synchronize()
+        dec.check()
+        assert _rel(l_peer.cpu().numpy(), l_ref.cpu().numpy()) <= 1e-2
+        assert _rel(l_nccl.cpu().numpy(), l_ref.cpu().numpy()) <= 1e-2
+        # the exchange inside a CUDA graph: the epoch advances on the device
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=s):
+                out = dec.step_logits(tok)
+            for _ in range(4):
+                gr.replay()
+            s.synchronize()
+        dec.check()
+        assert torch.equal(out.float(), l_peer)
+        del gr
+    finally:
+        dec.close()
+
+
+@pytest.mark.parametrize("which", ["exchange", "decoder"])
+def test_peer_exchange_two_gpus(which):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    mp.spawn(_worker, args=(2, _free_port(), which), nprocs=2, join=True)
