@@ -11,6 +11,10 @@ torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 
+# hidden 1024 = two 8x512 K-tiles, so o_proj splits over 2 ranks along whole heads
+SMALL_TP_CFG = dict(layers=2, hidden=1024, heads=8, head_dim=128, mlp=2048, vocab=1000, kv_len=64)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -86,7 +90,7 @@ def _exchange(rank, world, dev):
 def _decoder(rank, world, dev):
     from ecq_b200.model import Llama7BConfig, Llama7BDecoder
 
-    cfg = Llama7BConfig(layers=2, hidden=512, heads=4, head_dim=128, mlp=1024, vocab=1000, kv_len=64)
+    cfg = Llama7BConfig(**SMALL_TP_CFG)
     tok = torch.tensor([17], device=dev)
     ref = Llama7BDecoder(cfg, device=dev, tp=1, seed=5)
     l_ref = ref.step_logits(tok).float()

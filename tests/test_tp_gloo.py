@@ -110,3 +110,25 @@ def test_tp_partition_of_llama7b(tp):
         # gate/up rows are exactly the down_proj K-range
         assert p["mlp_slabs"][0] * 8 == p["down_ktiles"][0] * 256
         assert p["mlp_slabs"][1] * 8 == p["down_ktiles"][1] * 256
+
+
+@pytest.mark.parametrize("tp", [1, 2, 4, 8])
+def test_decoder_partition_lines_up(tp):
+    """The shard plan splits o_proj along whole heads and down_proj along the
+    rows gate|up produce, for the 7B shape at every TP size and for the small
+    configuration of the 2-GPU test."""
+    from ecq_b200.codec import choose_tile_cols
+    from ecq_b200.model import Llama7BConfig, tp_partition
+
+    small = dict(layers=2, hidden=1024, heads=8, head_dim=128, mlp=2048, vocab=1000, kv_len=64)
+    for cfg in (Llama7BConfig(), Llama7BConfig(**small)):
+        if tp > 2 and cfg.hidden == 1024:
+            continue
+        tc_h = choose_tile_cols(cfg.hidden, 128)
+        for plan in tp_partition(cfg, tp):
+            q0, q1 = plan["qkv_slabs"]
+            k0, k1 = plan["o_ktiles"]
+            assert (q1 - q0) * 8 == (k1 - k0) * tc_h and ((q1 - q0) * 8) % cfg.head_dim == 0
+            m0, m1 = plan["mlp_slabs"]
+            d0, d1 = plan["down_ktiles"]
+            assert (m1 - m0) * 8 == (d1 - d0) * choose_tile_cols(cfg.mlp, 128)
