@@ -18,46 +18,49 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* addr) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* addr) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
     return v;
 }
 
-// One CTA: wait for every rank's partials of this rank's epoch, sum them in
-// rank order, then h_out = h + d and y = rmsnorm(h_out) * w (the arithmetic
-// of ecq_add_rmsnorm_f16), and advance the epoch.
+// One CTA: sum every rank's partials of this rank's epoch e in rank order --
+// each slot is polled until its epoch half reads e + 1 (bounded: after ~1 s
+// the kernel sets ECQ_STATUS_TIMEOUT and stops waiting) -- then
+// h_out = h + d and y = rmsnorm(h_out) * w (the arithmetic of
+// ecq_add_rmsnorm_f16), and advance the epoch.
 __global__ void tp_add_rmsnorm_kernel(const __half* h, ecq_tp_comm c, const __half* __restrict__ w,
                                       __half* h_out, __half* __restrict__ y, int n, float eps,
                                       uint32_t* __restrict__ status) {
     extern __shared__ float buf[];  // n floats + 32 partials
-    __shared__ uint32_t s_epoch;
+    __shared__ uint32_t s_epoch, s_gave_up;
     uint32_t* epoch = static_cast<uint32_t*>(c.local);
     if (threadIdx.x == 0) {
-        const uint32_t e = *reinterpret_cast<volatile uint32_t*>(epoch);
-        s_epoch = e;
-        const uint32_t* flags = reinterpret_cast<const uint32_t*>(static_cast<const uint8_t*>(c.local) + 128u) +
-                                (e & 1u) * ECQ_TP_MAX_RANKS;
-        const uint64_t t0 = global_timer_ns();
-        bool timed_out = false;
-        for (uint32_t r = 0; r < c.world && !timed_out; ++r) {
-            while (ld_acquire_sys_u32(flags + r) != e + 1u) {
-                if (global_timer_ns() - t0 > kFlagWaitNs) {
-                    atomicOr(status, ECQ_STATUS_TIMEOUT);
-                    timed_out = true;
-                    break;
-                }
-            }
-        }
+        s_epoch = *reinterpret_cast<volatile uint32_t*>(epoch);
+        s_gave_up = 0u;
     }
     __syncthreads();
     const uint32_t e = s_epoch;
-    const float* part = reinterpret_cast<const float*>(static_cast<const uint8_t*>(c.local) + 256u) +
-                        static_cast<size_t>(e & 1u) * c.world * c.n_max;
+    const uint64_t* slot = reinterpret_cast<const uint64_t*>(static_cast<const uint8_t*>(c.local) + 256u) +
+                           static_cast<size_t>(e & 1u) * c.world * c.n_max;
+    const uint64_t t0 = global_timer_ns();
     float ss = 0.f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         float d = 0.f;
-        for (uint32_t r = 0; r < c.world; ++r) d += __ldcg(part + static_cast<size_t>(r) * c.n_max + i);
+        for (uint32_t r = 0; r < c.world; ++r) {
+            const uint64_t* a = slot + static_cast<size_t>(r) * c.n_max + i;
+            uint64_t v = ld_relaxed_sys_u64(a);
+            while (static_cast<uint32_t>(v >> 32) != e + 1u) {
+                if (*reinterpret_cast<volatile uint32_t*>(&s_gave_up)) break;
+                if (global_timer_ns() - t0 > kFlagWaitNs) {
+                    s_gave_up = 1u;
+                    atomicOr(status, ECQ_STATUS_TIMEOUT);
+                    break;
+                }
+                v = ld_relaxed_sys_u64(a);
+            }
+            d += __uint_as_float(static_cast<uint32_t>(v));
+        }
         const float v = __half2float(__float2half_rn(__half2float(h[i]) + __half2float(__float2half_rn(d))));
         buf[i] = v;
         ss += v * v;
@@ -78,7 +81,7 @@ __global__ void tp_add_rmsnorm_kernel(const __half* h, ecq_tp_comm c, const __ha
         h_out[i] = __float2half_rn(v);
         y[i] = __hmul(__float2half_rn(v * rs), w[i]);
     }
-    __syncthreads();  // every partial has been read
+    __syncthreads();  // every slot has been read
     if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(epoch) = e + 1u;
 }
 
@@ -97,7 +100,7 @@ extern "C" {
 
 int64_t ecq_comm_buffer_bytes(uint32_t n_max, uint32_t world) {
     if (n_max == 0 || world < 1 || world > ECQ_TP_MAX_RANKS) return ECQ_ERR_ARG;
-    return 256 + 2ll * world * n_max * static_cast<int64_t>(sizeof(float));
+    return 256 + 2ll * world * n_max * static_cast<int64_t>(sizeof(uint64_t));
 }
 
 int32_t ecq_comm_alloc(int64_t bytes, void** d_buf) {

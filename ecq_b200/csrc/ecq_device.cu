@@ -105,8 +105,7 @@ struct MatrixParams {
     // fp32 partials to every rank's exchange buffer instead of to p.y
     uint8_t* tp_peer[ECQ_TP_MAX_RANKS];
     uint32_t* tp_epoch;  // this rank's epoch counter
-    uint32_t* tp_done;   // row slabs finished in this launch (workspace)
-    uint32_t tp_world, tp_rank, tp_nmax, n_slabs;
+    uint32_t tp_world, tp_rank, tp_nmax;
 };
 
 // what matrix_kernel does with the decoded symbols
@@ -164,37 +163,23 @@ __device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* addr, uint32_t v)
     return old;
 }
 
-// Tensor-parallel push of one finished row slab: its fp32 row sums go to
-// partials[e & 1][rank][row] of every rank's exchange buffer (plain stores,
-// through CUDA IPC mappings for the peers), fenced at system scope; the warp
-// that finishes the launch's last slab then raises flags[e & 1][rank] = e + 1
-// on every rank with a system-scope release. Buffer layout: include/ecq_comm.h.
-__device__ __forceinline__ void st_release_sys_u32(uint32_t* addr, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+// Tensor-parallel push of one finished row slab: each row sum goes to
+// slot[e & 1][rank][row] of every rank's exchange buffer (through CUDA IPC
+// mappings for the peers) as ONE 8-byte store of (fp32 value, e + 1): the
+// consumer polls each slot until its epoch half reads e + 1, and an aligned
+// 8-byte store is never seen half-written, so no fence, counter or separate
+// flag is needed (the low-latency scheme of small all-reduces). Buffer
+// layout: include/ecq_comm.h.
+__device__ __forceinline__ void st_relaxed_sys_u64(uint8_t* addr, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t atom_add_acq_rel_sys(uint32_t* addr, uint32_t v) {
-    uint32_t old;
-    asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
-    return old;
-}
-__device__ __forceinline__ void tp_push_slab(const MatrixParams& p, uint32_t slab, int row, bool writer, float s,
-                                             int lane) {
+__device__ __forceinline__ void tp_push_slab(const MatrixParams& p, uint32_t slab, int row, bool writer, float s) {
+    if (!writer) return;
     const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(p.tp_epoch);
-    if (writer) {
-        const size_t off = 256u + ((static_cast<size_t>(e & 1u) * p.tp_world + p.tp_rank) * p.tp_nmax +
-                                   static_cast<size_t>(slab) * kTileRows + row) * sizeof(float);
-        for (uint32_t q = 0; q < p.tp_world; ++q) *reinterpret_cast<float*>(p.tp_peer[q] + off) = s;
-    }
-    __threadfence_system();
-    __syncwarp();
-    if (lane == 0) {
-        if (atom_add_acq_rel_sys(p.tp_done, 1u) == p.n_slabs - 1) {
-            *p.tp_done = 0u;  // read again by the next launch only
-            for (uint32_t q = 0; q < p.tp_world; ++q)
-                st_release_sys_u32(reinterpret_cast<uint32_t*>(p.tp_peer[q] + 128u) + (e & 1u) * ECQ_TP_MAX_RANKS + p.tp_rank,
-                                   e + 1u);
-        }
-    }
+    const size_t off = 256u + ((static_cast<size_t>(e & 1u) * p.tp_world + p.tp_rank) * p.tp_nmax +
+                               static_cast<size_t>(slab) * kTileRows + row) * sizeof(uint64_t);
+    const uint64_t v = (static_cast<uint64_t>(e + 1u) << 32) | __float_as_uint(s);
+    for (uint32_t q = 0; q < p.tp_world; ++q) st_relaxed_sys_u64(p.tp_peer[q] + off, v);
 }
 
 __device__ __forceinline__ void complete_pending(const MatrixParams& p, PendingSlab& pend, int lane) {
@@ -212,7 +197,7 @@ __device__ __forceinline__ void complete_pending(const MatrixParams& p, PendingS
         if (p.tp_world == 0) {
             if (kp == 0 && row < pend.rows) p.y[slab * kTileRows + row] = __float2half_rn(s);
         } else {
-            tp_push_slab(p, slab, row, kp == 0 && row < pend.rows, s, lane);
+            tp_push_slab(p, slab, row, kp == 0 && row < pend.rows, s);
         }
         if (lane == 0) p.slab_count[slab] = 0u;
     }
@@ -533,12 +518,10 @@ int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, cons
     p.flags = m->flags;
     // x staged by bulk copy needs a 16-byte aligned address
     p.x_bytes = (gemv && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) ? ls.x_bytes : 0u;
-    p.n_slabs = (m->rows + kTileRows - 1) / kTileRows;
     if (gemv) {
         p.partials = static_cast<float*>(workspace);
         p.slab_count = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) +
                                                    static_cast<size_t>(m->n_tiles) * kTileRows * sizeof(float));
-        p.tp_done = p.slab_count + p.n_slabs;
     }
     if (comm) {
         p.tp_world = comm->world;
@@ -597,8 +580,7 @@ int64_t ecq_gemv_workspace_bytes(const ecq_matrix_view* m, uint32_t batch) {
     (void)batch;
     if (!m || !m->rows || !m->n_tiles) return ECQ_ERR_ARG;
     const int64_t slabs = (m->rows + kTileRows - 1) / kTileRows;
-    // per-tile row partials, per-slab counters, one launch-wide slab counter (padded)
-    return static_cast<int64_t>(m->n_tiles) * kTileRows * 4 + slabs * 4 + 16;
+    return static_cast<int64_t>(m->n_tiles) * kTileRows * 4 + slabs * 4;
 }
 
 int32_t ecq_gemv(const ecq_matrix_view* m, const void* x_f16, const void* scales_f16, void* y_f16, uint32_t batch,

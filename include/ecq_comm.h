@@ -2,10 +2,10 @@
  * ecq_comm.h -- the tensor-parallel exchange of a batch-1 decode step, fused
  * into the kernels on either side of it: the row-parallel fused GEMV pushes
  * its fp32 partial y straight into every peer GPU's receive buffer over
- * NVLink (plain peer stores into CUDA-IPC-mapped memory, no multicast) and
- * raises a per-epoch flag there once its last row slab is done; the next
- * kernel (residual add + RMSNorm) waits for all ranks' flags with a bounded
- * wait and sums the partials in rank order. It replaces the NCCL all-reduce
+ * NVLink (plain peer stores into CUDA-IPC-mapped memory, no multicast), each
+ * value stored together with its epoch in one 8-byte word; the next kernel
+ * (residual add + RMSNorm) polls those words with a bounded wait and sums the
+ * partials in rank order. It replaces the NCCL all-reduce
  * (sum) that closes every row-parallel layer of the tensor-parallel step
  * (the reference's model glue lives in its MLX fork; the layer structure is
  * experiments/real_model_test.py:18-113).
@@ -30,9 +30,9 @@ extern "C" {
 #define ECQ_IPC_HANDLE_BYTES 64
 
 /* Exchange-buffer layout (bytes from its base): [0, 4) this rank's epoch
- * counter; [128, 192) flags[2][8] (u32, written by peers: the epoch + 1 whose
- * partials have arrived); [256, ...) partials[2][world][n_max] (fp32, written
- * by peers). Index [e & 1] alternates with the epoch e. */
+ * counter; [256, ...) slots[2][world][n_max], u64, written by the ranks:
+ * fp32 value bits | (epoch + 1) << 32. Index [e & 1] alternates with the
+ * epoch e; a slot is valid for epoch e once its high half reads e + 1. */
 typedef struct ecq_tp_comm {
     uint32_t world;   /* ranks, 1..ECQ_TP_MAX_RANKS */
     uint32_t rank;    /* this rank */
@@ -57,16 +57,15 @@ int32_t ecq_ipc_open(const void *handle /* ECQ_IPC_HANDLE_BYTES */, void **d_map
 int32_t ecq_ipc_close(void *d_mapped);
 
 /* The fused GEMV of a row-parallel layer at batch 1 (x [cols], scales as for
- * ecq_gemv): instead of writing y, each row slab's fp32 sums go to
- * partials[e & 1][rank][row] on every rank, and once the launch's last slab is
- * done flags[e & 1][rank] = e + 1 on every rank (e = this rank's epoch).
- * rows <= n_max. The workspace is ecq_gemv_workspace_bytes(m, 1) bytes. */
+ * ecq_gemv): instead of writing y, each row's fp32 sum goes to
+ * slots[e & 1][rank][row] on every rank as (value, e + 1) in one 8-byte store
+ * (e = this rank's epoch). rows <= n_max. The workspace is ecq_gemv_workspace_bytes(m, 1) bytes. */
 int32_t ecq_gemv_tp(const ecq_matrix_view *m, const void *x_f16, const void *scales_f16, const ecq_tp_comm *comm,
                     void *workspace, int64_t workspace_bytes, uint32_t *d_status, void *stream);
 
 /* The consumer: wait (bounded, ~1 s; ECQ_STATUS_TIMEOUT on expiry) until
- * every rank's flag for this rank's epoch e is up, then d = sum over ranks of
- * partials[e & 1][r][0..n) (rank order, fp32, rounded once to fp16),
+ * every rank's slots [e & 1][r][0..n) read e + 1 (e = this rank's epoch), then
+ * d = sum over ranks of their values (rank order, fp32, rounded once to fp16),
  * h_out = h + d and y = rmsnorm(h_out) * w as ecq_add_rmsnorm_f16 does for
  * one row, and advance the epoch. n <= n_max, n <= 12256. */
 int32_t ecq_tp_add_rmsnorm_f16(const void *h, const ecq_tp_comm *comm, const void *w, void *h_out, void *y, int32_t n,

@@ -29,7 +29,7 @@ def test_library_exports_all_symbols():
 
 def test_workspace_size_query_is_host_only():
     v = _lib.MatrixView(rows=4096, cols=4096, tile_rows=8, tile_cols=512, group_size=128, n_tiles=4096)
-    assert _lib.lib().ecq_gemv_workspace_bytes(v, 1) == 4096 * 8 * 4 + 512 * 4 + 16  # partials, slab and launch counters
+    assert _lib.lib().ecq_gemv_workspace_bytes(v, 1) == 4096 * 8 * 4 + 512 * 4
 
 
 def test_tp_comm_struct_mirrors_header():
@@ -37,5 +37,5 @@ def test_tp_comm_struct_mirrors_header():
 
     assert ctypes.sizeof(_lib.TPComm) == 4 * 4 + 8 + 8 * _lib.TP_MAX_RANKS
     assert _lib.TPComm.local.offset == 16 and _lib.TPComm.peers.offset == 24
-    assert _lib.lib().ecq_comm_buffer_bytes(4096, 8) == 256 + 2 * 8 * 4096 * 4
+    assert _lib.lib().ecq_comm_buffer_bytes(4096, 8) == 256 + 2 * 8 * 4096 * 8  # (value, epoch) words
     assert _lib.lib().ecq_comm_buffer_bytes(4096, 9) < 0  # more ranks than the exchange holds
