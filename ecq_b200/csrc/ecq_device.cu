@@ -138,14 +138,6 @@ __device__ __forceinline__ float transpose_reduce8(float (&v)[8], int lane) {
     return v[0];
 }
 
-// Lane l < NSG holds the scale of scale-group l of this tile row (the NSG
-// groups a tile row spans); the others hold 0.
-template <int NSG, int GPL>
-__device__ __forceinline__ float load_row_scale(const MatrixParams& p, uint32_t row, uint32_t c0, int lane) {
-    if (lane >= NSG) return 0.f;
-    return __half2float(p.scales[static_cast<size_t>(row) * p.ng + (c0 + lane * GPL * 32) / p.group_size]);
-}
-
 // Row-slab completion. A tile's 8 row sums go to the workspace and lane 0
 // bumps the slab's counter with an acquire-release atomic; the warp does not
 // wait for the atomic's result: it checks it after its next tile (or at the
@@ -255,8 +247,23 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
     constexpr bool SCALED = MODE != kModeSymbols;  // needs the group scales
     float xs[MPL];  // x * 2^-14 (exact), this lane's columns of the tile
     float acc[kTileRows];
-    float sc = 0.f;
-    if constexpr (MODE == kModeWeights) sc = load_row_scale<NSG, GPL>(p, r0, c0, lane) * 6.103515625e-05f;
+    // Every group scale of the tile, loaded once up front (one load per lane
+    // instead of a dependent load per row): value v = r * NSG + sg (row r,
+    // group sg) sits in lane v % 32 of sca[v / 32]; rows past the matrix read 0.
+    constexpr int NSR = (kTileRows * NSG + 31) / 32;
+    float sca[NSR];
+    if constexpr (SCALED) {
+        const uint32_t g0 = c0 / p.group_size;  // the tile's first group column
+#pragma unroll
+        for (int k = 0; k < NSR; ++k) {
+            const int v = 32 * k + lane;
+            const int r = v / NSG;
+            float s = 0.f;
+            if (r < rows_here) s = __half2float(p.scales[static_cast<size_t>(r0 + r) * p.ng + g0 + (v % NSG)]);
+            if constexpr (MODE == kModeWeights) s *= 6.103515625e-05f;  // scale * 2^-14
+            sca[k] = s;
+        }
+    }
     if constexpr (GEMV) {
 #pragma unroll
         for (int m = 0; m < MPL; ++m) {
@@ -267,16 +274,21 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
         }
 #pragma unroll
         for (int r = 0; r < kTileRows; ++r) acc[r] = 0.f;
-        sc = load_row_scale<NSG, GPL>(p, r0, c0, lane);
     }
 
 #pragma unroll 1
     for (int r = 0; r < rows_here; ++r) {
         float rowacc = 0.f;
-        float sn = 0.f;
+        float sreg = 0.f;  // the register of sca holding row r's scales
         if constexpr (SCALED) {
-            if (r + 1 < rows_here) sn = load_row_scale<NSG, GPL>(p, r0 + r + 1, c0, lane);
-            if constexpr (MODE == kModeWeights) sn *= 6.103515625e-05f;  // scale * 2^-14
+            if constexpr (NSR == 1) {
+                sreg = sca[0];
+            } else {
+                const int k = (r * NSG) >> 5;
+                sreg = sca[0];
+#pragma unroll
+                for (int kk = 1; kk < NSR; ++kk) sreg = k == kk ? sca[kk] : sreg;
+            }
         }
 #pragma unroll
         for (int sg = 0; sg < NSG; ++sg) {
@@ -297,7 +309,7 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
                 part = lo + hi;
             } else {
                 float gscale = 0.f;
-                if constexpr (MODE == kModeWeights) gscale = __shfl_sync(0xffffffffu, sc, sg);
+                if constexpr (MODE == kModeWeights) gscale = __shfl_sync(0xffffffffu, sreg, (r * NSG + sg) & 31);
                 (void)gscale;
 #pragma unroll
                 for (int mm = 0; mm < GPL; ++mm) {
@@ -319,14 +331,13 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
                     }
                 }
             }
-            if constexpr (GEMV) rowacc = fmaf(__shfl_sync(0xffffffffu, sc, sg), part, rowacc);
+            if constexpr (GEMV) rowacc = fmaf(__shfl_sync(0xffffffffu, sreg, (r * NSG + sg) & 31), part, rowacc);
         }
         if constexpr (GEMV) {
 #pragma unroll
             for (int k = 0; k < kTileRows - 1; ++k) acc[k] = acc[k + 1];
             acc[kTileRows - 1] = rowacc;
         }
-        if constexpr (SCALED) sc = sn;
     }
     if constexpr (!CONSTANT) {
         if (x != kL || (a - buf - lane) != len * 32u) atomicOr(p.status, ECQ_STATUS_CORRUPT);
