@@ -8,8 +8,13 @@
 #include <string.h>
 
 #include "ecq_comm.h"
+#include "ecq_kernels.cuh"
 
 namespace {
+
+using ecq_dev::launch_pdl;
+using ecq_dev::pdl_launch_dependents;
+using ecq_dev::pdl_wait;
 
 constexpr uint64_t kFlagWaitNs = 1000ull * 1000ull * 1000ull;  // 1 s
 
@@ -35,6 +40,8 @@ __global__ void tp_add_rmsnorm_kernel(const __half* h, ecq_tp_comm c, const __ha
     extern __shared__ float buf[];  // n floats + 32 partials
     __shared__ uint32_t s_epoch, s_gave_up;
     uint32_t* epoch = static_cast<uint32_t*>(c.local);
+    pdl_launch_dependents();
+    pdl_wait();  // h and this rank's epoch come from the kernels before this one
     if (threadIdx.x == 0) {
         s_epoch = *reinterpret_cast<volatile uint32_t*>(epoch);
         s_gave_up = 0u;
@@ -148,10 +155,15 @@ int32_t ecq_tp_add_rmsnorm_f16(const void* h, const ecq_tp_comm* comm, const voi
         static_cast<uint32_t>(n) > comm->n_max)
         return ECQ_ERR_ARG;
     const int threads = n >= 1024 ? 1024 : ((n + 31) / 32) * 32;
-    tp_add_rmsnorm_kernel<<<1, threads, (n + 32) * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __half*>(h), *comm, static_cast<const __half*>(w), static_cast<__half*>(h_out),
-        static_cast<__half*>(y), n, eps, d_status);
-    return cudaGetLastError() == cudaSuccess ? ECQ_OK : ECQ_ERR_CUDA;
+    const cudaError_t rc = launch_pdl(tp_add_rmsnorm_kernel, dim3(1), dim3(threads), (n + 32) * sizeof(float),
+                                      static_cast<cudaStream_t>(stream), static_cast<const __half*>(h), *comm,
+                                      static_cast<const __half*>(w), static_cast<__half*>(h_out),
+                                      static_cast<__half*>(y), n, eps, d_status);
+    if (rc != cudaSuccess) {
+        cudaGetLastError();
+        return ECQ_ERR_CUDA;
+    }
+    return ECQ_OK;
 }
 
 }  // extern "C"

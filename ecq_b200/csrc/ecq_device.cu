@@ -362,6 +362,7 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
     const uint32_t table_bar = smem_addr(bars + 2 * W);
     const bool constant = p.flags & ECQ_FLAG_CONSTANT;
 
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2 * W + 1; ++i) mbar_init(smem_addr(bars + i), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -373,7 +374,6 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
         for (int i = 0; i < 4; ++i)
             bulk_copy_g2s(sbase + i * (kTableBytes / 4), reinterpret_cast<const uint8_t*>(p.dec_table) + i * (kTableBytes / 4),
                           kTableBytes / 4, table_bar);
-        if (p.x_bytes) bulk_copy_g2s(sbase + kTableBytes, p.x, p.x_bytes, table_bar);
     }
 
     // contiguous run of tiles for this warp
@@ -399,6 +399,11 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
     };
 
     if (lane == 0 && t_begin < t_end) issue(t_begin, 0);
+    // x, the outputs and the workspace may belong to the kernel before this
+    // one in the stream: wait for it only now, with the table and the first
+    // tile on their way
+    pdl_wait();
+    if (threadIdx.x == 0 && p.x_bytes) bulk_copy_g2s(sbase + kTableBytes, p.x, p.x_bytes, table_bar);
     bool ok = mbar_wait(table_bar, 0);
     if (!ok && lane == 0) atomicOr(p.status, ECQ_STATUS_TIMEOUT);
 
@@ -544,8 +549,11 @@ int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, cons
     KernelFn fn = gemv ? pick_kernel<kModeGemv>(ls.mpl, ls.gpl)
                        : (w_out ? pick_kernel<kModeWeights>(ls.mpl, ls.gpl) : pick_kernel<kModeSymbols>(ls.mpl, ls.gpl));
     if (!ensure_smem_limit(reinterpret_cast<const void*>(fn), kMaxSmem)) return ECQ_ERR_CUDA;
-    fn<<<ls.ctas, ls.warps * 32, ls.smem, stream>>>(p);
-    return cudaGetLastError() == cudaSuccess ? ECQ_OK : ECQ_ERR_CUDA;
+    if (launch_pdl(fn, dim3(ls.ctas), dim3(ls.warps * 32), ls.smem, stream, p) != cudaSuccess) {
+        cudaGetLastError();
+        return ECQ_ERR_CUDA;
+    }
+    return ECQ_OK;
 }
 
 bool view_ok(const ecq_matrix_view* m) {

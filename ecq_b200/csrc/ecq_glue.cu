@@ -10,13 +10,20 @@
 #include <stdint.h>
 
 #include "ecq_glue.h"
+#include "ecq_kernels.cuh"
 
 namespace {
+
+using ecq_dev::launch_pdl;
+using ecq_dev::pdl_launch_dependents;
+using ecq_dev::pdl_wait;
 
 __global__ void add_rmsnorm_kernel(const __half* __restrict__ h, const __half* __restrict__ d,
                                    const __half* __restrict__ w, __half* __restrict__ h_out, __half* __restrict__ y,
                                    int n, float eps) {
     extern __shared__ float buf[];  // n floats + 32 partials
+    pdl_launch_dependents();
+    pdl_wait();  // h and d come from the kernels before this one
     const size_t row = blockIdx.x;
     h += row * n;
     if (d) d += row * n;
@@ -51,6 +58,8 @@ __global__ void add_rmsnorm_kernel(const __half* __restrict__ h, const __half* _
 __global__ void rope_kv_kernel(__half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
                                __half* __restrict__ kc, __half* __restrict__ vc, const __half* __restrict__ cs,
                                const __half* __restrict__ sn, int heads, int dim, int64_t cache_head_stride) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int h = blockIdx.x;
     const int half_dim = dim / 2;
     for (int i = threadIdx.x; i < half_dim; i += blockDim.x) {
@@ -70,6 +79,8 @@ __global__ void rope_kv_kernel(__half* __restrict__ q, const __half* __restrict_
 }
 
 __global__ void silu_mul_kernel(const __half* __restrict__ gu, __half* __restrict__ m, int f, int64_t rows) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int64_t n = static_cast<int64_t>(f) * rows;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -88,29 +99,31 @@ int32_t ecq_add_rmsnorm_f16(const void* h, const void* d, const void* w, void* h
                             int32_t n, float eps, void* stream) {
     if (!h || !w || !y || rows < 1 || n < 1 || (d && !h_out) || n > 12256) return -1;
     const int threads = n >= 1024 ? 1024 : ((n + 31) / 32) * 32;
-    add_rmsnorm_kernel<<<rows, threads, (n + 32) * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const __half*>(h), static_cast<const __half*>(d), static_cast<const __half*>(w),
-        static_cast<__half*>(h_out), static_cast<__half*>(y), n, eps);
-    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+    const cudaError_t rc = launch_pdl(add_rmsnorm_kernel, dim3(rows), dim3(threads), (n + 32) * sizeof(float),
+                                      static_cast<cudaStream_t>(stream), static_cast<const __half*>(h),
+                                      static_cast<const __half*>(d), static_cast<const __half*>(w),
+                                      static_cast<__half*>(h_out), static_cast<__half*>(y), n, eps);
+    return rc == cudaSuccess ? 0 : (cudaGetLastError(), -6);
 }
 
 int32_t ecq_rope_kv_f16(void* q, const void* k, const void* v, void* k_cache, void* v_cache, const void* cos_t,
                         const void* sin_t, int32_t heads, int32_t dim, int64_t cache_head_stride, void* stream) {
     if (!q || !k || !v || !k_cache || !v_cache || !cos_t || !sin_t || heads < 1 || dim < 2 || (dim & 1)) return -1;
-    rope_kv_kernel<<<heads, 64, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<__half*>(q), static_cast<const __half*>(k), static_cast<const __half*>(v),
-        static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), static_cast<const __half*>(cos_t),
-        static_cast<const __half*>(sin_t), heads, dim, cache_head_stride);
-    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+    const cudaError_t rc = launch_pdl(rope_kv_kernel, dim3(heads), dim3(64), 0, static_cast<cudaStream_t>(stream),
+                                      static_cast<__half*>(q), static_cast<const __half*>(k),
+                                      static_cast<const __half*>(v), static_cast<__half*>(k_cache),
+                                      static_cast<__half*>(v_cache), static_cast<const __half*>(cos_t),
+                                      static_cast<const __half*>(sin_t), heads, dim, cache_head_stride);
+    return rc == cudaSuccess ? 0 : (cudaGetLastError(), -6);
 }
 
 int32_t ecq_silu_mul_f16(const void* gate_up, void* m, int32_t f, int32_t rows, void* stream) {
     if (!gate_up || !m || f < 1 || rows < 1) return -1;
     const int64_t n = static_cast<int64_t>(f) * rows;
     const int blocks = static_cast<int>((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184);
-    silu_mul_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<const __half*>(gate_up),
-                                                                            static_cast<__half*>(m), f, rows);
-    return cudaGetLastError() == cudaSuccess ? 0 : -6;
+    const cudaError_t rc = launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                                      static_cast<const __half*>(gate_up), static_cast<__half*>(m), f, n / f);
+    return rc == cudaSuccess ? 0 : (cudaGetLastError(), -6);
 }
 
 }  // extern "C"

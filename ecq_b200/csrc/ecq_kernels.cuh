@@ -157,6 +157,37 @@ __host__ __device__ constexpr uint32_t overrun_pad() {
     return (32u * (5u + 3u * kTileRows * MPL) + 127u) & ~127u;
 }
 
+// Programmatic dependent launch. A kernel launched with launch_pdl may start
+// while the kernel before it in the stream is still running: it does the work
+// that needs nothing from that kernel first (barrier set-up, decode-table and
+// tile copies) and calls pdl_wait() before it touches anything the earlier
+// kernel may write or read (activations, outputs, workspaces). pdl_wait()
+// returns once the earlier kernel has completed and its writes are visible.
+// pdl_launch_dependents() lets the next such kernel start early; it may be
+// called at entry, because the next kernel waits for this one's completion
+// before touching its data, and it only runs once every CTA of this grid has
+// been scheduled.
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Raise a kernel's dynamic shared-memory limit once per (kernel, device),
 // outside any stream capture that may follow.
 inline bool ensure_smem_limit(const void* fn, int bytes) {
