@@ -57,6 +57,7 @@ def parse():
     ap.add_argument("--llama-steps", type=int, default=20)
     ap.add_argument("--no-batched", action="store_true", help="skip the 70B-MLP batched-token config")
     ap.add_argument("--no-sweep", action="store_true", help="skip the 8192x8192 entropy sweep")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the column-sharded sweep (N > 1)")
     return ap.parse_args()
 
 
@@ -389,6 +390,11 @@ def run_ecq(args):
     if not args.no_sweep and world == 1:
         sweep = run_entropy_sweep(dev)
 
+    sharded = None
+    if world > 1 and not args.no_sharded:
+        sharded = run_sharded_sweep(inputs, dev, world, rank, barrier,
+                                    {f"{M}x{K}": round(v * 1e3, 2) for (M, K), v in zip(SHAPES, avg_ms)})
+
     llama = None
     if not args.no_llama:
         del step_graph, launch_graphs
@@ -427,6 +433,7 @@ def run_ecq(args):
         "llama7b_decode": llama,
         "batched_70b_mlp": batched,
         "entropy_sweep_8192": sweep,
+        "column_sharded_sweep": sharded,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
@@ -539,6 +546,83 @@ def run_batched(dev, world=1, rank=0, barrier=None):
         out["batches"][str(B)] = row
     m.check()
     return out
+
+
+def run_sharded_sweep(inputs, dev, world, rank, barrier, per_shape_us):
+    """The sweep's three shapes split over the ranks, each whole matrix once
+    per call: K-split (every rank a share of the K-tiles) summed over the
+    ranks by the fused peer exchange (GEMV push + sum kernel) and, for
+    comparison, by an NCCL all-reduce; and row-split (every rank a share of
+    the row slabs) followed by an NCCL all-gather. CUDA events, max over
+    ranks, median of 10 calls each preceded by a 256 MB L2 flush. The fused
+    K-split result is checked against the unsharded GEMV first."""
+    import torch
+    import torch.distributed as dist
+
+    import ecq_b200 as ecq
+    from ecq_b200.codec import slice_matrix, split_even
+    from ecq_b200.comm import PeerExchange
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    xch = PeerExchange(n_max=max(d["M"] for d in inputs), device=dev)
+    out = {}
+
+    def timed(fn):
+        ms = _median_ms(fn, flush, barrier=barrier)
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    try:
+        for (M, K), d in zip(SHAPES, inputs):
+            enc = d["enc"]
+            nk, ns = K // enc.tile_cols, (M + 7) // 8
+            kt0, kt1 = split_even(nk, world)[rank]
+            s0, s1 = split_even(ns, world)[rank]
+            c0, c1 = kt0 * enc.tile_cols, kt1 * enc.tile_cols
+            mk = ecq.DeviceMatrix.from_encoded(slice_matrix(enc, 0, ns, kt0, kt1), group_size=GROUP, device=dev)
+            sk = torch.from_numpy(np.ascontiguousarray(d["scales"][:, c0 // GROUP:c1 // GROUP])).to(dev)
+            xk = torch.from_numpy(np.ascontiguousarray(d["x"][:, c0:c1])).to(dev)
+            mr = ecq.DeviceMatrix.from_encoded(slice_matrix(enc, s0, s1, 0, nk), group_size=GROUP, device=dev)
+            sr = torch.from_numpy(np.ascontiguousarray(d["scales"][s0 * 8:min(s1 * 8, M)])).to(dev)
+            x = torch.from_numpy(d["x"]).to(dev)
+            rows_max = max(min(b * 8, M) - a * 8 for a, b in split_even(ns, world))
+            yr = torch.zeros(1, rows_max, dtype=torch.float16, device=dev)
+            yg = torch.empty(world, rows_max, dtype=torch.float16, device=dev)
+            yk = torch.empty(M, dtype=torch.float16, device=dev)
+
+            def fused():
+                xch.gemv_push(mk, xk, sk)
+                return xch.sum(M, out=yk)
+
+            def nccl():
+                y = mk.gemv(xk, sk)
+                dist.all_reduce(y)
+                return y
+
+            def rows():
+                mr.gemv(x, sr, out=yr[:, : mr.rows])
+                dist.all_gather_into_tensor(yg, yr)
+                return yg
+
+            y_full = ecq.DeviceMatrix.from_encoded(enc, group_size=GROUP, device=dev).gemv(
+                x, torch.from_numpy(d["scales"]).to(dev))
+            y_f = fused().clone()
+            torch.cuda.synchronize()
+            xch.check()
+            err = float((y_f.float() - y_full[0].float()).abs().max() / y_full.float().abs().max())
+            assert err <= 2e-3, f"sharded parity gate failed for {M}x{K}: {err}"
+            res = {"k_split_fused_us": round(1e3 * timed(fused), 2), "k_split_nccl_us": round(1e3 * timed(nccl), 2),
+                   "row_split_allgather_us": round(1e3 * timed(rows), 2),
+                   "one_gpu_us": per_shape_us.get(f"{M}x{K}"), "max_rel_err": round(err, 6)}
+            res["effective_4bit_gbs_fused"] = round(M * K / 2 / (res["k_split_fused_us"] / 1e6) / 1e9, 1)
+            out[f"{M}x{K}"] = res
+            mk.check()
+            mr.check()
+    finally:
+        xch.close()
+    return {"n_gpus": world, "shapes": out,
+            "split": "K-tiles (fused exchange or NCCL all-reduce) / row slabs (NCCL all-gather)"}
 
 
 def run_entropy_sweep(dev):

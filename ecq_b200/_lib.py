@@ -59,6 +59,7 @@ EXPORTS = (
     "ecq_ipc_close",
     "ecq_gemv_tp",
     "ecq_tp_add_rmsnorm_f16",
+    "ecq_tp_sum_f16",
     "ecq_add_rmsnorm_f16",
     "ecq_rope_kv_f16",
     "ecq_silu_mul_f16",
@@ -120,6 +121,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "ecq_ipc_close": (c_int32, [P]),
         "ecq_gemv_tp": (c_int32, [POINTER(MatrixView), P, P, POINTER(TPComm), P, c_int64, P, P]),
         "ecq_tp_add_rmsnorm_f16": (c_int32, [P, POINTER(TPComm), P, P, P, c_int32, ctypes.c_float, P, P]),
+        "ecq_tp_sum_f16": (c_int32, [POINTER(TPComm), P, c_int32, P, P]),
         "ecq_add_rmsnorm_f16": (c_int32, [P, P, P, P, P, c_int32, c_int32, ctypes.c_float, P]),
         "ecq_rope_kv_f16": (c_int32, [P, P, P, P, P, P, P, c_int32, c_int32, c_int64, P]),
         "ecq_silu_mul_f16": (c_int32, [P, P, c_int32, c_int32, P]),

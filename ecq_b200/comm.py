@@ -75,6 +75,15 @@ class PeerExchange:
                                            torch.cuda.current_stream(self.device).cuda_stream), "tp_add_rmsnorm")
         return y
 
+    def sum(self, n: int, out: torch.Tensor | None = None) -> torch.Tensor:
+        """y [n] fp16 = sum over ranks of this epoch's partials (after every
+        rank's gemv_push): the all-reduce of a column-sharded GEMV."""
+        if out is None:
+            out = torch.empty(n, dtype=torch.float16, device=self.device)
+        check(lib().ecq_tp_sum_f16(ctypes.byref(self.desc), ptr(out), int(n), ptr(self.status),
+                                   torch.cuda.current_stream(self.device).cuda_stream), "tp_sum")
+        return out
+
     def check(self) -> None:
         s = int(self.status.item())
         if s:

@@ -92,6 +92,45 @@ __global__ void tp_add_rmsnorm_kernel(const __half* h, ecq_tp_comm c, const __ha
     if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(epoch) = e + 1u;
 }
 
+// One CTA: y[i] = sum over ranks of this rank's epoch-e slots (rank order,
+// fp32, rounded once to fp16), waiting for each slot as above; then advance
+// the epoch. The plain all-reduce that closes a column-sharded GEMV.
+__global__ void tp_sum_kernel(ecq_tp_comm c, __half* __restrict__ y, int n, uint32_t* __restrict__ status) {
+    __shared__ uint32_t s_epoch, s_gave_up;
+    uint32_t* epoch = static_cast<uint32_t*>(c.local);
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x == 0) {
+        s_epoch = *reinterpret_cast<volatile uint32_t*>(epoch);
+        s_gave_up = 0u;
+    }
+    __syncthreads();
+    const uint32_t e = s_epoch;
+    const uint64_t* slot = reinterpret_cast<const uint64_t*>(static_cast<const uint8_t*>(c.local) + 256u) +
+                           static_cast<size_t>(e & 1u) * c.world * c.n_max;
+    const uint64_t t0 = global_timer_ns();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        float d = 0.f;
+        for (uint32_t r = 0; r < c.world; ++r) {
+            const uint64_t* a = slot + static_cast<size_t>(r) * c.n_max + i;
+            uint64_t v = ld_relaxed_sys_u64(a);
+            while (static_cast<uint32_t>(v >> 32) != e + 1u) {
+                if (*reinterpret_cast<volatile uint32_t*>(&s_gave_up)) break;
+                if (global_timer_ns() - t0 > kFlagWaitNs) {
+                    s_gave_up = 1u;
+                    atomicOr(status, ECQ_STATUS_TIMEOUT);
+                    break;
+                }
+                v = ld_relaxed_sys_u64(a);
+            }
+            d += __uint_as_float(static_cast<uint32_t>(v));
+        }
+        y[i] = __float2half_rn(d);
+    }
+    __syncthreads();  // every slot has been read
+    if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(epoch) = e + 1u;
+}
+
 bool comm_ok(const ecq_tp_comm* c) {
     if (!c || c->world < 1 || c->world > ECQ_TP_MAX_RANKS || c->rank >= c->world || !c->local) return false;
     for (uint32_t q = 0; q < c->world; ++q)
@@ -159,6 +198,17 @@ int32_t ecq_tp_add_rmsnorm_f16(const void* h, const ecq_tp_comm* comm, const voi
                                       static_cast<cudaStream_t>(stream), static_cast<const __half*>(h), *comm,
                                       static_cast<const __half*>(w), static_cast<__half*>(h_out),
                                       static_cast<__half*>(y), n, eps, d_status);
+    if (rc != cudaSuccess) {
+        cudaGetLastError();
+        return ECQ_ERR_CUDA;
+    }
+    return ECQ_OK;
+}
+
+int32_t ecq_tp_sum_f16(const ecq_tp_comm* comm, void* y, int32_t n, uint32_t* d_status, void* stream) {
+    if (!y || !d_status || !comm_ok(comm) || n < 1 || static_cast<uint32_t>(n) > comm->n_max) return ECQ_ERR_ARG;
+    const cudaError_t rc = launch_pdl(tp_sum_kernel, dim3(1), dim3(1024), 0, static_cast<cudaStream_t>(stream), *comm,
+                                      static_cast<__half*>(y), n, d_status);
     if (rc != cudaSuccess) {
         cudaGetLastError();
         return ECQ_ERR_CUDA;

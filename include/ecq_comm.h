@@ -71,6 +71,12 @@ int32_t ecq_gemv_tp(const ecq_matrix_view *m, const void *x_f16, const void *sca
 int32_t ecq_tp_add_rmsnorm_f16(const void *h, const ecq_tp_comm *comm, const void *w, void *h_out, void *y, int32_t n,
                                float eps, uint32_t *d_status, void *stream);
 
+/* The plain consumer: y[0..n) = sum over ranks of this rank's epoch-e slots
+ * (rank order, fp32, rounded once to fp16), waiting as above, then advance
+ * the epoch. ecq_gemv_tp followed by this is a column-sharded GEMV with its
+ * all-reduce fused in. n <= n_max. */
+int32_t ecq_tp_sum_f16(const ecq_tp_comm *comm, void *y, int32_t n, uint32_t *d_status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

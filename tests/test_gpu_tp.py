@@ -83,6 +83,15 @@ def _exchange(rank, world, dev):
             y_ref = (hf / np.sqrt(np.mean(hf * hf) + 1e-5)).astype(np.float16).astype(np.float32) * \
                 w.float().cpu().numpy()
             assert _rel(y.float().cpu().numpy(), y_ref) <= 2e-3, it
+        for it in range(3):  # the plain all-reduce consumer, continuing the epochs
+            x = syn.activations(1, K, seed=90 + it)
+            xch.gemv_push(m, torch.from_numpy(np.ascontiguousarray(x[0, c0:c1])).to(dev), s_loc)
+            y = xch.sum(M)
+            torch.cuda.synchronize()
+            m.check()
+            xch.check()
+            d = oracle.dequant_gemv(sym, sc.astype(np.float32), g, x.astype(np.float32))[0]
+            assert y.shape == (M,) and _rel(y.float().cpu().numpy(), d) <= 2e-3, it
     finally:
         xch.close()
 
