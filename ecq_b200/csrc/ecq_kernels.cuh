@@ -120,14 +120,16 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
 // Renormalisation reads the next two bytes ahead of need and shifts in 0, 1
 // or 2 of them with one funnel shift. After a decode step of an intact
 // stream 2^9 <= x < 2^31, and the reference's byte loop reads one byte iff
-// x < 2^23 and a second iff x < 2^15. (A damaged stream may need a third,
-// which is not read; the end-of-stream check flags it.)
+// x < 2^23 and a second iff x < 2^15: the shift is clz(2x) & 24 bits
+// (clz(2x) = clz(x) - 1 lies in [0,7], [8,15] or [16,21] for the three
+// cases). A damaged stream can leave x below 2^9; the shift is then at most
+// 24 bits (3 bytes, the read-ahead bound the callers pad for), the state is
+// wrong from there on, and the end-of-stream check flags the tile.
 __device__ __forceinline__ uint32_t decode_step(uint32_t& x, uint32_t& a, uint32_t tb) {
     uint32_t e;
     asm volatile(
         "{\n\t"
         ".reg .u32 b0, b1, sl, q, f, bi, nx, sh;\n\t"
-        ".reg .pred p1, p2;\n\t"
         "ld.shared.u8 b0, [%1];\n\t"          // next two stream bytes, read ahead of need
         "ld.shared.u8 b1, [%1+32];\n\t"
         "and.b32 sl, %0, 16383;\n\t"          // slot
@@ -138,10 +140,9 @@ __device__ __forceinline__ uint32_t decode_step(uint32_t& x, uint32_t& a, uint32
         "and.b32 bi, %2, 16383;\n\t"
         "mad.lo.u32 %0, f, q, bi;\n\t"        // x = freq * (x >> 14) + slot - cumfreq
         "prmt.b32 nx, b1, b0, 0x4011;\n\t"    // b0 << 24 | b1 << 16
-        "setp.lt.u32 p1, %0, 8388608;\n\t"    // x < 2^23: one byte due
-        "setp.lt.u32 p2, %0, 32768;\n\t"      // x < 2^15: two bytes due
-        "selp.u32 sh, 8, 0, p1;\n\t"
-        "selp.u32 sh, 16, sh, p2;\n\t"
+        "shl.b32 sh, %0, 1;\n\t"             // x < 2^31 here, so clz(2x) = clz(x) - 1
+        "clz.b32 sh, sh;\n\t"
+        "and.b32 sh, sh, 24;\n\t"           // 0, 8 or 16: x >= 2^23, >= 2^15, < 2^15
         "shf.l.wrap.b32 %0, nx, %0, sh;\n\t"  // x = (x << sh) | (nx >> (32 - sh))
         "mad.lo.u32 %1, sh, 4, %1;\n\t"       // 32 bytes per consumed byte
         "}"
