@@ -55,7 +55,12 @@ class DeviceMatrix:
         data = np.ascontiguousarray(enc.data)
         if data.size == 0:
             data = np.zeros(16, dtype=np.uint8)
-        to = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a).view(dt)).to(dev)
+        def to(a, dt):
+            a = np.ascontiguousarray(a)
+            if not a.flags.writeable:  # e.g. a memory-mapped container blob: torch wants writable host memory
+                a = a.copy()
+            return torch.from_numpy(a.view(dt)).to(dev)
+
         m = cls(rows=enc.rows, cols=enc.cols, tile_rows=enc.tile_rows, tile_cols=enc.tile_cols,
                 group_size=int(group_size), table=enc.table, flags=flags, max_tile_bytes=enc.max_tile_bytes,
                 data=to(data, np.uint8), tile_offset=to(enc.tile_offset.astype(np.uint32), np.int32),
