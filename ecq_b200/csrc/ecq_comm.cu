@@ -29,6 +29,36 @@ __device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* addr) {
     return v;
 }
 
+// Sum over ranks of slot i of epoch half `slot` (want = e + 1 in the high
+// halves): every rank's word is loaded first and only then checked, so an
+// element costs one round trip to memory, not one per rank; a word not yet
+// written is polled again until it is or the wait gives up (bounded, shared
+// flag, status bit).
+__device__ __forceinline__ float sum_ranks(const uint64_t* slot, const ecq_tp_comm& c, int i, uint32_t want,
+                                           uint64_t t0, uint32_t* gave_up, uint32_t* status) {
+    uint64_t v[ECQ_TP_MAX_RANKS];
+#pragma unroll
+    for (int r = 0; r < ECQ_TP_MAX_RANKS; ++r)
+        if (r < static_cast<int>(c.world)) v[r] = ld_relaxed_sys_u64(slot + static_cast<size_t>(r) * c.n_max + i);
+    float d = 0.f;
+#pragma unroll
+    for (int r = 0; r < ECQ_TP_MAX_RANKS; ++r) {
+        if (r < static_cast<int>(c.world)) {
+            while (static_cast<uint32_t>(v[r] >> 32) != want) {
+                if (*reinterpret_cast<volatile uint32_t*>(gave_up)) break;
+                if (global_timer_ns() - t0 > kFlagWaitNs) {
+                    *gave_up = 1u;
+                    atomicOr(status, ECQ_STATUS_TIMEOUT);
+                    break;
+                }
+                v[r] = ld_relaxed_sys_u64(slot + static_cast<size_t>(r) * c.n_max + i);
+            }
+            d += __uint_as_float(static_cast<uint32_t>(v[r]));
+        }
+    }
+    return d;
+}
+
 // One CTA: sum every rank's partials of this rank's epoch e in rank order --
 // each slot is polled until its epoch half reads e + 1 (bounded: after ~1 s
 // the kernel sets ECQ_STATUS_TIMEOUT and stops waiting) -- then
@@ -53,21 +83,7 @@ __global__ void tp_add_rmsnorm_kernel(const __half* h, ecq_tp_comm c, const __ha
     const uint64_t t0 = global_timer_ns();
     float ss = 0.f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float d = 0.f;
-        for (uint32_t r = 0; r < c.world; ++r) {
-            const uint64_t* a = slot + static_cast<size_t>(r) * c.n_max + i;
-            uint64_t v = ld_relaxed_sys_u64(a);
-            while (static_cast<uint32_t>(v >> 32) != e + 1u) {
-                if (*reinterpret_cast<volatile uint32_t*>(&s_gave_up)) break;
-                if (global_timer_ns() - t0 > kFlagWaitNs) {
-                    s_gave_up = 1u;
-                    atomicOr(status, ECQ_STATUS_TIMEOUT);
-                    break;
-                }
-                v = ld_relaxed_sys_u64(a);
-            }
-            d += __uint_as_float(static_cast<uint32_t>(v));
-        }
+        const float d = sum_ranks(slot, c, i, e + 1u, t0, &s_gave_up, status);
         const float v = __half2float(__float2half_rn(__half2float(h[i]) + __half2float(__float2half_rn(d))));
         buf[i] = v;
         ss += v * v;
@@ -110,21 +126,7 @@ __global__ void tp_sum_kernel(ecq_tp_comm c, __half* __restrict__ y, int n, uint
                            static_cast<size_t>(e & 1u) * c.world * c.n_max;
     const uint64_t t0 = global_timer_ns();
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float d = 0.f;
-        for (uint32_t r = 0; r < c.world; ++r) {
-            const uint64_t* a = slot + static_cast<size_t>(r) * c.n_max + i;
-            uint64_t v = ld_relaxed_sys_u64(a);
-            while (static_cast<uint32_t>(v >> 32) != e + 1u) {
-                if (*reinterpret_cast<volatile uint32_t*>(&s_gave_up)) break;
-                if (global_timer_ns() - t0 > kFlagWaitNs) {
-                    s_gave_up = 1u;
-                    atomicOr(status, ECQ_STATUS_TIMEOUT);
-                    break;
-                }
-                v = ld_relaxed_sys_u64(a);
-            }
-            d += __uint_as_float(static_cast<uint32_t>(v));
-        }
+        const float d = sum_ranks(slot, c, i, e + 1u, t0, &s_gave_up, status);
         y[i] = __float2half_rn(d);
     }
     __syncthreads();  // every slot has been read
