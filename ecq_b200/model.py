@@ -82,9 +82,34 @@ class ShardedLinear:
         return rans_gemv(x, self.m, self.scales)
 
 
-def _encode_shards(parts, table: RANSTable, tile_cols: int, device) -> ShardedLinear:
+# A batch-1 GEMV whose shard has fewer tiles than the GPU has warps (about
+# 4.7K) waits on one tile's serial decode: narrower tiles shorten that chain
+# but cost per-tile overhead and compression. Measured on TP-8 shard shapes,
+# the best width is the widest one that still gives this many tiles.
+MIN_TILES = 2048
+
+
+def shard_tile_cols(rows: int, cols: int, group: int = GROUP, min_tiles: int = MIN_TILES) -> int:
+    """Tile width for encoding one [rows, cols] shard: the widest of
+    512 / 256 / 128 columns compatible with cols and the group size that
+    gives at least `min_tiles` 8-row tiles (else the narrowest compatible)."""
+    ok = [c for c in (512, 256, 128) if cols % c == 0 and (c % group == 0 if group < c else group % c == 0)]
+    if not ok:
+        raise ValueError(f"no tile width for {cols} columns, group {group}")
+    for c in ok:
+        if ((rows + 7) // 8) * (cols // c) >= min_tiles:
+            return c
+    return ok[-1]
+
+
+def _encode_shards(parts, table: RANSTable, tile_cols: int | None, device) -> ShardedLinear:
     """Encode the row blocks `parts` = [(symbols, scales, (r0, r1), (c0, c1)), ...]
-    with one shared table and stack them into one packed matrix."""
+    with one shared table and stack them into one packed matrix (tile width
+    `tile_cols`, or chosen by shard_tile_cols for the stacked shape)."""
+    if tile_cols is None:
+        rows = sum(r1 - r0 for _, _, (r0, r1), _ in parts)
+        c0, c1 = parts[0][3]
+        tile_cols = shard_tile_cols(rows, c1 - c0)
     encs, scs = [], []
     for q_full, sc_full, (r0, r1), (c0, c1) in parts:
         block = q_full[r0:r1, c0:c1].contiguous().cpu().numpy()
@@ -145,15 +170,15 @@ class Llama7BDecoder:
                 W[name] = quantized_student_t(M, K, seed=s, device=self.dev)
                 s += 1
             t_qkv = _table_of(W["q"][0], W["k"][0], W["v"][0])
-            lw["qkv"] = _encode_shards([(W[n][0], W[n][1], hr, (0, H)) for n in ("q", "k", "v")], t_qkv, tc_h,
+            lw["qkv"] = _encode_shards([(W[n][0], W[n][1], hr, (0, H)) for n in ("q", "k", "v")], t_qkv, None,
                                        self.dev)
             lw["o"] = _encode_shards([(W["o"][0], W["o"][1], (0, H), (kt_o[0] * tc_h, kt_o[1] * tc_h))],
-                                     _table_of(W["o"][0]), tc_h, self.dev)
+                                     _table_of(W["o"][0]), None, self.dev)
             t_gu = _table_of(W["gate"][0], W["up"][0])
-            lw["gate_up"] = _encode_shards([(W[n][0], W[n][1], mr, (0, H)) for n in ("gate", "up")], t_gu, tc_h,
+            lw["gate_up"] = _encode_shards([(W[n][0], W[n][1], mr, (0, H)) for n in ("gate", "up")], t_gu, None,
                                            self.dev)
             lw["down"] = _encode_shards([(W["down"][0], W["down"][1], (0, H), (kt_d[0] * tc_m, kt_d[1] * tc_m))],
-                                        _table_of(W["down"][0]), tc_m, self.dev)
+                                        _table_of(W["down"][0]), None, self.dev)
             del W
             for k in ("qkv", "o", "gate_up", "down"):
                 self.compressed_bytes += lw[k].m.compressed_bytes
@@ -163,7 +188,7 @@ class Llama7BDecoder:
             self.layers.append(lw)
         q, sc = quantized_student_t(cfg.vocab, H, seed=s, device=self.dev)
         vr = (vocab_slabs[0] * 8, min(vocab_slabs[1] * 8, cfg.vocab))
-        self.lm_head = _encode_shards([(q, sc, vr, (0, H))], _table_of(q), tc_h, self.dev)
+        self.lm_head = _encode_shards([(q, sc, vr, (0, H))], _table_of(q), None, self.dev)
         self.compressed_bytes += self.lm_head.m.compressed_bytes
         self.symbols += self.lm_head.m.rows * self.lm_head.m.cols
         del q, sc
@@ -282,4 +307,5 @@ def tp_partition(cfg: Llama7BConfig, tp: int) -> list[dict]:
     return plans
 
 
-__all__ = ["Llama7BConfig", "Llama7BDecoder", "tp_partition", "quantized_student_t", "math", "_lib", "np"]
+__all__ = ["Llama7BConfig", "Llama7BDecoder", "tp_partition", "shard_tile_cols", "quantized_student_t", "math", "_lib",
+           "np"]

@@ -132,3 +132,19 @@ def test_decoder_partition_lines_up(tp):
             m0, m1 = plan["mlp_slabs"]
             d0, d1 = plan["down_ktiles"]
             assert (m1 - m0) * 8 == (d1 - d0) * choose_tile_cols(cfg.mlp, 128)
+
+
+def test_shard_tile_widths():
+    """Shards keep 8x512 tiles while they have >= 2048 tiles and narrow them
+    when they have fewer (the latency-bound TP-8 shards); widths always
+    divide the shard's columns and fit group 128."""
+    from ecq_b200.model import shard_tile_cols
+
+    assert shard_tile_cols(12288, 4096) == 512      # q|k|v, TP 1
+    assert shard_tile_cols(4096, 11008) == 256      # down, TP 1 (11008 is not a multiple of 512)
+    assert shard_tile_cols(1536, 4096) == 256       # q|k|v, TP 8
+    assert shard_tile_cols(4096, 512) == 128        # o, TP 8
+    assert shard_tile_cols(3072, 4096) == 512       # gate|up, TP 8
+    for rows, cols in ((8, 128), (1000, 384), (4096, 1408)):
+        c = shard_tile_cols(rows, cols)
+        assert cols % c == 0 and c % 128 == 0 or c == 128
