@@ -214,3 +214,23 @@ def test_entropy_sweep_8192(b):
         m.check()
         y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), gs, x.astype(np.float32))
         assert _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL, gs
+
+
+def test_gemv_with_unaligned_x():
+    """x that does not start on a 16-byte boundary cannot be bulk-copied into
+    shared memory: the kernel then reads it from global memory. Same result."""
+    M, K = 136, 1024
+    sym = syn.laplace_symbols(M, K, b=0.5, seed=21)
+    sc = torch.from_numpy(syn.group_scales(M, K, 128, seed=22)).cuda()
+    x = syn.activations(1, K, seed=23)
+    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, group_size=128), group_size=128)
+    buf = torch.zeros(K + 8, dtype=torch.float16, device="cuda")
+    buf[1:K + 1] = torch.from_numpy(x[0]).cuda()
+    xu = buf[1:K + 1].view(1, K)  # 2 bytes past an aligned address
+    assert xu.data_ptr() % 16 != 0
+    y_u = m.gemv(xu, sc)
+    y_a = m.gemv(torch.from_numpy(x).cuda(), sc)
+    m.check()
+    assert torch.equal(y_u, y_a)
+    y_ref = oracle.dequant_gemv(sym, sc.float().cpu().numpy(), 128, x.astype(np.float32))
+    assert _rel_err(y_u.float().cpu().numpy(), y_ref) <= RTOL
