@@ -55,7 +55,10 @@ class PackedTensor:
         from .device import DeviceMatrix
 
         m = DeviceMatrix.from_encoded(self.enc, group_size=self.group_size, device=device)
-        return m, torch.from_numpy(np.ascontiguousarray(self.scales)).to(device)
+        sc = np.ascontiguousarray(self.scales)
+        if not sc.flags.writeable:  # a memory-mapped blob: torch wants writable host memory
+            sc = sc.copy()
+        return m, torch.from_numpy(sc).to(device)
 
 
 def _pad(n: int) -> int:
