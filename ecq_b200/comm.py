@@ -88,7 +88,9 @@ class PeerExchange:
         s = int(self.status.item())
         if s:
             self.status.zero_()
-            raise _lib.EcqError(f"peer exchange status {s:#x} (a rank's partials did not arrive in time)")
+            # the ranks' epochs may now disagree: close() and rebuild the exchange on every rank
+            raise _lib.EcqError(f"peer exchange status {s:#x} (a rank's partials did not arrive in time; "
+                                "rebuild the exchange on every rank)")
 
     def close(self) -> None:
         """Release the mappings and the buffer. Every rank must be done with

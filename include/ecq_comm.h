@@ -67,7 +67,9 @@ int32_t ecq_gemv_tp(const ecq_matrix_view *m, const void *x_f16, const void *sca
  * every rank's slots [e & 1][r][0..n) read e + 1 (e = this rank's epoch), then
  * d = sum over ranks of their values (rank order, fp32, rounded once to fp16),
  * h_out = h + d and y = rmsnorm(h_out) * w as ecq_add_rmsnorm_f16 does for
- * one row, and advance the epoch. n <= n_max, n <= 12256. */
+ * one row, and advance the epoch. n <= n_max, n <= 12256. After a timeout
+ * the ranks' epochs may disagree: the results are unusable and every rank
+ * must rebuild its exchange buffer before the next exchange. */
 int32_t ecq_tp_add_rmsnorm_f16(const void *h, const ecq_tp_comm *comm, const void *w, void *h_out, void *y, int32_t n,
                                float eps, uint32_t *d_status, void *stream);
 
