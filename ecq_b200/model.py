@@ -23,14 +23,11 @@ all-reduces.
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 
-import numpy as np
 import torch
 import torch.distributed as dist
 
-from . import _lib
 from ._lib import check, lib
 from .codec import RANSTable, concat_rows, encode_matrix, split_even, choose_tile_cols
 from .device import DeviceMatrix
@@ -307,5 +304,4 @@ def tp_partition(cfg: Llama7BConfig, tp: int) -> list[dict]:
     return plans
 
 
-__all__ = ["Llama7BConfig", "Llama7BDecoder", "tp_partition", "shard_tile_cols", "quantized_student_t", "math", "_lib",
-           "np"]
+__all__ = ["Llama7BConfig", "Llama7BDecoder", "tp_partition", "shard_tile_cols", "quantized_student_t"]
