@@ -1,7 +1,6 @@
 """The Llama-shaped decode step (model.py) on a small configuration, TP = 1:
 logits from the rANS-coded fused GEMVs against the same step computed with
 plain fp32 matmuls on the dequantised weights."""
-import numpy as np
 import pytest
 
 torch = pytest.importorskip("torch")
