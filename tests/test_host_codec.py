@@ -122,3 +122,59 @@ def test_choose_tile_cols():
     assert ecq.choose_tile_cols(4096, 64) == 512
     with pytest.raises(ValueError):
         ecq.choose_tile_cols(100, 128)
+
+
+def test_split_even():
+    """Even partition of K-tiles / row slabs over ranks: contiguous, covering,
+    sizes differing by at most one with the larger parts first."""
+    from ecq_b200.codec import split_even
+
+    for n in (0, 1, 7, 43, 512):
+        for parts in (1, 2, 3, 8):
+            r = split_even(n, parts)
+            assert len(r) == parts and r[0][0] == 0 and r[-1][1] == n
+            sizes = [b - a for a, b in r]
+            assert all(r[i][1] == r[i + 1][0] for i in range(parts - 1))
+            assert max(sizes) - min(sizes) <= 1 and sizes == sorted(sizes, reverse=True)
+
+
+@pytest.mark.parametrize("s0,s1,k0,k1", [(0, 5, 0, 3), (1, 4, 1, 2), (4, 5, 2, 3), (0, 5, 2, 3)])
+def test_slice_matrix_is_the_sub_block(s0, s1, k0, k1):
+    """A slice of a packed matrix (row slabs x K-tiles, same tile bytes) runs
+    through the reference CPU path like the same block of symbols."""
+    from ecq_b200.codec import slice_matrix
+
+    rows, cols, tc, g = 36, 768, 256, 128
+    sym = syn.laplace_symbols(rows, cols, b=0.5, seed=31)
+    sc = syn.group_scales(rows, cols, g, seed=32).astype(np.float32)
+    x = syn.activations(1, cols, seed=33).astype(np.float32)
+    enc = ecq.encode_matrix(sym, tile_cols=tc, group_size=g)
+    part = slice_matrix(enc, s0, s1, k0, k1)
+    r0, r1, c0, c1 = s0 * 8, min(s1 * 8, rows), k0 * tc, k1 * tc
+    assert (part.rows, part.cols) == (r1 - r0, c1 - c0)
+    sub_sc = np.ascontiguousarray(sc[r0:r1, c0 // g:c1 // g])
+    y, bad = oracle.gemv_packed(part.data, part.tile_offset, part.stream_len, part.rows, part.cols, 8, tc,
+                                enc.table.freq, sub_sc, g, x[:, c0:c1])
+    assert bad == 0
+    y_ref = oracle.dequant_gemv(sym[r0:r1, c0:c1], sub_sc, g, x[:, c0:c1])[0]
+    assert np.allclose(y, y_ref, rtol=1e-5, atol=1e-5)
+
+
+def test_concat_rows_stacks_matrices():
+    """Packed matrices that share columns, tile width and table stack into one
+    (the fused q|k|v and gate|up projections)."""
+    from ecq_b200.codec import concat_rows
+
+    cols, tc, g = 512, 256, 128
+    a = syn.laplace_symbols(16, cols, b=0.5, seed=41)
+    b = syn.laplace_symbols(13, cols, b=0.5, seed=42)
+    t = ecq.RANSTable.from_symbols(np.concatenate([a, b]))
+    enc = concat_rows([ecq.encode_matrix(a, t, tile_cols=tc, group_size=g),
+                       ecq.encode_matrix(b, t, tile_cols=tc, group_size=g)])
+    both = np.concatenate([a, b])
+    assert (enc.rows, enc.cols) == both.shape
+    sc = syn.group_scales(*both.shape, g, seed=43).astype(np.float32)
+    x = syn.activations(1, cols, seed=44).astype(np.float32)
+    y, bad = oracle.gemv_packed(enc.data, enc.tile_offset, enc.stream_len, enc.rows, cols, 8, tc, t.freq, sc, g, x)
+    assert bad == 0
+    assert np.allclose(y, oracle.dequant_gemv(both, sc, g, x)[0], rtol=1e-5, atol=1e-5)
