@@ -84,6 +84,26 @@ def algorithmic_bytes(enc, M, K, B=1):
             + 2 * M * ng + 2 * B * K + 2 * B * M)
 
 
+def issue_roofline(symbols_per_s, shapes, inst_executed, sm_count, sm_mhz):
+    """Symbols/s against the integer-issue ceiling of the decode.
+
+    Each SM has 4 schedulers, each issuing at most one warp instruction per
+    cycle, and one warp instruction advances 32 lanes (32 streams). The
+    decode's cost is the warp instructions one launch executes
+    (`inst_executed`, ncu `smsp__inst_executed.sum` per shape "MxK"), so
+    ceiling = sm_count * 4 * clock * 32 / (instructions per 32 symbols),
+    with the instructions per 32 symbols weighted over the sweep's shapes.
+    Returns None when a shape has no instruction count."""
+    if not inst_executed or any(f"{M}x{K}" not in inst_executed for M, K in shapes):
+        return None
+    inst = sum(float(inst_executed[f"{M}x{K}"]) for M, K in shapes)
+    sym = sum(M * K for M, K in shapes)
+    per32 = inst / (sym / 32.0)
+    ceiling = sm_count * 4 * sm_mhz * 1e6 * 32.0 / per32
+    return {"inst_per_32_symbols": round(per32, 2), "sm_count": sm_count, "sm_mhz": sm_mhz,
+            "ceiling_symbols_per_s": round(ceiling, 1), "frac": round(symbols_per_s / ceiling, 4)}
+
+
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
 
@@ -407,6 +427,15 @@ def run_ecq(args):
 
     comp_bytes_step = R * sum(algorithmic_bytes(d0["enc"], d0["M"], d0["K"]) for d0 in inputs)
     ms_step = ms_max / args.steps
+    clk = clocks.summary()
+    issue = None
+    try:
+        inst = json.loads((ROOT / "profiles" / "gemv_issue.json").read_text()).get("inst_executed")
+        issue = issue_roofline(sym_per_step / (ms_step / 1e3), SHAPES, inst,
+                               torch.cuda.get_device_properties(dev).multi_processor_count,
+                               float(clk.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)))
+    except (OSError, ValueError):
+        issue = None
     line = {
         "metric": "fused decode+GEMV effective 4-bit weight GB/s", "value": round(value, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -427,6 +456,7 @@ def run_ecq(args):
             "compressed_gbs": round(comp_bytes_step / (ms_step / 1e3) / 1e9, 2),
             "symbols_per_s": round(sym_per_step / (ms_step / 1e3), 1),
             "plain_4bit_roofline_gbs": hbm_peak,
+            "issue_roofline": issue,
         },
         "e2e": e2e,
         "cpu_baseline": cpu,
@@ -435,7 +465,7 @@ def run_ecq(args):
         "entropy_sweep_8192": sweep,
         "column_sharded_sweep": sharded,
         "gpu_launches": launches_per_step * args.steps,
-        "clocks": clocks.summary(),
+        "clocks": clk,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -1,0 +1,49 @@
+"""Host-only checks of bench.py's derived views (no GPU): the integer-issue
+roofline of the decode and the committed instruction counts it reads."""
+import importlib.util
+import json
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def bench():
+    spec = importlib.util.spec_from_file_location("bench", ROOT / "bench.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_issue_roofline_arithmetic(bench):
+    # 32 instructions per 32 symbols: one symbol per lane-instruction, so the
+    # ceiling is 4 schedulers x 32 lanes x clock per SM
+    shapes = [(64, 512), (128, 256)]
+    inst = {"64x512": 64 * 512, "128x256": 128 * 256}
+    r = bench.issue_roofline(1e12, shapes, inst, sm_count=148, sm_mhz=2000.0)
+    assert r["inst_per_32_symbols"] == pytest.approx(32.0)
+    assert r["ceiling_symbols_per_s"] == pytest.approx(148 * 4 * 2e9)
+    assert r["frac"] == pytest.approx(1e12 / (148 * 4 * 2e9), rel=1e-3)
+
+
+def test_issue_roofline_weights_shapes_by_symbols(bench):
+    shapes = [(32, 32), (32, 96)]
+    inst = {"32x32": 10 * 32, "32x96": 30 * 3 * 32}  # 10 and 30 instructions per 32 symbols
+    r = bench.issue_roofline(1.0, shapes, inst, sm_count=1, sm_mhz=1.0)
+    assert r["inst_per_32_symbols"] == pytest.approx((10 * 1 + 30 * 3) / 4)
+
+
+def test_issue_roofline_needs_every_shape(bench):
+    assert bench.issue_roofline(1.0, [(8, 8)], {"8x16": 1}, 1, 1.0) is None
+    assert bench.issue_roofline(1.0, [(8, 8)], None, 1, 1.0) is None
+
+
+def test_committed_instruction_counts_cover_the_sweep(bench):
+    inst = json.loads((ROOT / "profiles" / "gemv_issue.json").read_text())["inst_executed"]
+    r = bench.issue_roofline(0.84e12, bench.SHAPES, inst, sm_count=148, sm_mhz=1965.0)
+    assert r is not None
+    # the ncu capture counts 24.5-27.4 warp instructions per 32 symbols per shape
+    assert 20.0 < r["inst_per_32_symbols"] < 30.0
+    assert 0.0 < r["frac"] < 1.0
