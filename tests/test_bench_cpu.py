@@ -47,3 +47,18 @@ def test_committed_instruction_counts_cover_the_sweep(bench):
     # the ncu capture counts 24.5-27.4 warp instructions per 32 symbols per shape
     assert 20.0 < r["inst_per_32_symbols"] < 30.0
     assert 0.0 < r["frac"] < 1.0
+
+
+def test_cpu_baseline_runs_until_its_time_bound(bench):
+    # one small matrix through the oracle's decode + dequant + matvec
+    import ecq_b200 as ecq
+    from ecq_b200 import synthetic as syn
+
+    M, K = 64, 1024
+    sym = syn.laplace_symbols(M, K, b=0.5, seed=0)
+    d = dict(M=M, K=K, sym=sym, scales=syn.group_scales(M, K, bench.GROUP, seed=1),
+             x=syn.activations(1, K, seed=2), enc=ecq.encode_matrix(sym, group_size=bench.GROUP))
+    gbs, secs, sweeps = bench.cpu_baseline([d], threads=1, repeats=2, min_seconds=0.05)
+    assert sweeps >= 2 and secs >= 0.05 and gbs > 0
+    gbs1, secs1, sweeps1 = bench.cpu_baseline([d], threads=1, repeats=1)
+    assert sweeps1 == 1 and secs1 > 0 and gbs1 > 0
