@@ -219,6 +219,32 @@ class EncodedMatrix:
     def bits_per_symbol(self) -> float:
         return 8.0 * self.compressed_bytes / (self.rows * self.cols)
 
+    def validate(self) -> None:
+        """Reject an inconsistent tile index before anything reaches the
+        device. The kernels bulk-copy tile t from data + tile_offset[t] and
+        cannot see the blob's length, so offsets from an untrusted file must
+        start at 0, never decrease and end inside the data; a tile's size must
+        be a whole number of 32-byte stream rows, and the tile and stream
+        counts must match the shape. Raises ValueError."""
+        if self.tile_rows != _lib.TILE_ROWS or self.tile_cols <= 0 or self.tile_cols % 32 or self.cols % self.tile_cols:
+            raise ValueError("unsupported tile shape")
+        n_slabs = (self.rows + self.tile_rows - 1) // self.tile_rows
+        n_tiles = n_slabs * (self.cols // self.tile_cols)
+        off = np.asarray(self.tile_offset).astype(np.int64)
+        if off.ndim != 1 or off.size != n_tiles + 1:
+            raise ValueError("tile_offset must hold n_tiles + 1 entries")
+        if np.asarray(self.stream_len).size != 32 * n_tiles:
+            raise ValueError("stream_len must hold 32 entries per tile")
+        if off[0] != 0:
+            raise ValueError("tile_offset[0] must be 0")
+        sizes = np.diff(off)
+        if np.any(sizes < 0):
+            raise ValueError("tile offsets decrease")
+        if np.any(sizes % 32):
+            raise ValueError("a tile's size is not a multiple of 32 bytes")
+        if int(off[-1]) > int(np.asarray(self.data).size):
+            raise ValueError("tile offsets run past the data")
+
     def tile(self, t: int) -> InterleavedEncodedTile:
         """Tile t as a reference InterleavedEncodedTile."""
         o0, o1 = int(self.tile_offset[t]), int(self.tile_offset[t + 1])

@@ -125,10 +125,10 @@ def load_ecq2(path, mmap: bool = True) -> dict:
         enc = EncodedMatrix(rows=rows, cols=cols, tile_rows=t["tile_rows"], tile_cols=t["tile_cols"], table=table,
                             data=blob("data", np.uint8), tile_offset=blob("tile_offset", "<u4"),
                             stream_len=blob("stream_len", "<u2"))
-        if enc.n_tiles != ((rows + enc.tile_rows - 1) // enc.tile_rows) * (cols // enc.tile_cols):
-            raise ValueError(f"{name}: tile count does not match the shape")
-        if int(enc.tile_offset[-1]) > enc.data.size:
-            raise ValueError(f"{name}: tile offsets run past the data blob")
+        try:
+            enc.validate()
+        except ValueError as exc:
+            raise ValueError(f"{name}: {exc}") from None
         scales = blob("scales", "<f2").reshape(rows, (cols + g - 1) // g)
         out[name] = PackedTensor(enc=enc, scales=scales, group_size=g, meta=t.get("extra", {}))
     if len(out) != n:

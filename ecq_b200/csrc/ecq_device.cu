@@ -659,31 +659,71 @@ int32_t ecq_device_info(int32_t* sm_count, int32_t* gemv_ctas, int32_t* gemv_war
 // The array is a file-scope __device__ variable: every GPU that loads the
 // library holds ECQ_NOALLOC_SCRATCH_BYTES of it until the process exits.
 // From host code its name is only a host-side stand-in, never a device
-// address, so the device address is looked up once per device with
-// cudaGetSymbolAddress and cached. All calls share the one array, so two
-// calls whose kernels overlap on the GPU (different streams, or different
-// host threads) race on it and must be ordered by the caller.
+// address, so the device address is looked up with cudaGetSymbolAddress once
+// per device (with that device current) and cached together with the id of
+// the CUDA context it was found in: after cudaDeviceReset the module is
+// loaded again into a new context, possibly elsewhere, and the address is
+// looked up again. All calls share the one array, so two calls whose kernels
+// overlap on the GPU (different streams, or different host threads) race on
+// it and must be ordered by the caller.
 // ---------------------------------------------------------------------------
+struct CUctx_st;  // the driver's opaque context type (CUcontext)
+
 static __device__ __align__(256) uint8_t g_noalloc_scratch[ECQ_NOALLOC_SCRATCH_BYTES];
 
 namespace {
 
 constexpr int kMaxDevices = 64;
 
-// Device address of g_noalloc_scratch on the current device; resolved on the
-// first call for that device (with that device current) and cached.
+// Unique id (cuCtxGetId) of the CUDA context current on this thread, 0 when
+// there is none yet or the driver does not offer the query. The driver entry
+// points are fetched through the runtime, so libecq needs no libcuda link.
+unsigned long long current_context_id() {
+    using CtxCurrentFn = int (*)(CUctx_st**);
+    using CtxIdFn = int (*)(CUctx_st*, unsigned long long*);
+    static CtxCurrentFn ctx_current = nullptr;
+    static CtxIdFn ctx_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            ctx_current = reinterpret_cast<CtxCurrentFn>(f);
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            ctx_id = reinterpret_cast<CtxIdFn>(f);
+    });
+    if (!ctx_current || !ctx_id) return 0;
+    CUctx_st* c = nullptr;
+    if (ctx_current(&c) != 0 || !c) return 0;
+    unsigned long long id = 0;
+    return ctx_id(c, &id) == 0 ? id : 0;
+}
+
+// Device address of g_noalloc_scratch on the current device: looked up on
+// the first call for that device (with that device current) and again
+// whenever the current context is not the one the cached address came from.
 int32_t noalloc_scratch(void** out) {
+    struct Entry {
+        void* addr;
+        unsigned long long ctx;
+    };
     static std::mutex mu;
-    static void* addr[kMaxDevices] = {};
+    static Entry cache[kMaxDevices] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ECQ_ERR_CUDA;
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    Entry& e = cache[dev];
+    if (!e.addr || ctx == 0 || e.ctx != ctx) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return ECQ_ERR_CUDA;
-        addr[dev] = p;
+        e.addr = p;
+        e.ctx = ctx ? ctx : current_context_id();  // the lookup made the context current
     }
-    *out = addr[dev];
+    *out = e.addr;
     return ECQ_OK;
 }
 
@@ -698,9 +738,12 @@ extern "C" int32_t ecq_gemv_noalloc(const ecq_matrix_view* m, const void* x_f16,
     void* scratch = nullptr;
     const int32_t rc = noalloc_scratch(&scratch);
     if (rc != ECQ_OK) return rc;
-    // The per-slab completion counters (after the per-tile partial sums) must
-    // start at zero. A finished call leaves them zero, but the array keeps
-    // whatever the last call left, including one that failed: clear them.
+    // The per-slab completion counters follow the per-tile partial sums, so
+    // where they sit depends on this matrix's tile count: a call on a smaller
+    // matrix after a larger one finds its counters inside the larger one's
+    // partial sums, and a call that failed may leave counters set. Clear them
+    // on every call (the partial sums need no clearing: each is written
+    // before it is read).
     const int64_t counters = static_cast<int64_t>(m->n_tiles) * kTileRows * static_cast<int64_t>(sizeof(float));
     if (cudaMemsetAsync(static_cast<uint8_t*>(scratch) + counters, 0, static_cast<size_t>(need - counters),
                         static_cast<cudaStream_t>(stream)) != cudaSuccess)

@@ -50,6 +50,7 @@ class DeviceMatrix:
 
     @classmethod
     def from_encoded(cls, enc: EncodedMatrix, group_size: int = 128, device="cuda") -> "DeviceMatrix":
+        enc.validate()  # offsets from a file are checked before any device copy
         entries, flags = enc.table.decode_table()
         dev = torch.device(device)
         data = np.ascontiguousarray(enc.data)
@@ -67,8 +68,6 @@ class DeviceMatrix:
                 stream_len=to(enc.stream_len.astype(np.uint16), np.int16), dec_table=to(entries, np.int32),
                 workspace=torch.zeros(0, dtype=torch.uint8, device=dev),
                 status=torch.zeros(1, dtype=torch.int32, device=dev))
-        if int(enc.tile_offset[-1]) > enc.data.size:
-            raise ValueError("tile offsets run past the data")
         ws = lib().ecq_gemv_workspace_bytes(ctypes_view(m), 1)
         check(ws, "workspace size")
         m.workspace = torch.zeros(int(ws), dtype=torch.uint8, device=dev)

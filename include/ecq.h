@@ -72,6 +72,14 @@ extern "C" {
  * always a multiple of 32); stream_len[32*t + j] is stream j's byte length.
  * dec_table is the 16384-entry packed decode table from
  * ecq_build_decode_table for the matrix's frequency table.
+ *
+ * Precondition on tile_offset (the view carries no data length, so the
+ * kernels cannot check it): tile_offset[0] == 0, the offsets never decrease,
+ * every tile's size is a multiple of 32 bytes and at most max_tile_bytes, and
+ * tile_offset[n_tiles] does not exceed the data allocation. Check offsets
+ * read from an untrusted file on the host before building a view: a tile
+ * larger than max_tile_bytes is refused on the device (ECQ_STATUS_BADARG),
+ * but offsets past the end of the data make the bulk copies read outside it.
  */
 typedef struct ecq_matrix_view {
     uint32_t rows, cols;
@@ -186,12 +194,17 @@ int32_t ecq_gemv(const ecq_matrix_view *m, const void *x_f16, const void *scales
  *
  * The workspace comes from a fixed array inside the library
  * (ECQ_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the library until
- * exit), so matrices whose ecq_gemv_workspace_bytes exceed it are rejected
- * with ECQ_ERR_WORKSPACE: up to about 127K tiles (e.g. 28672 x 8192 in
- * 8x512 tiles). Nothing is allocated, by the library or anyone else. The
- * first call on each device looks up the array's device address
- * (cudaGetSymbolAddress, with that device current); make that first call
- * before any stream capture. Every call shares the array: calls whose
+ * exit). A matrix fits when ecq_gemv_workspace_bytes(m, 1) =
+ * n_tiles * 32 + ceil(rows / 8) * 4 <= ECQ_NOALLOC_SCRATCH_BYTES (between
+ * ~116.5K tiles, one K-tile per row slab, and ~130K, 16 per slab; e.g.
+ * 28672 x 8192 in 8x512 tiles); larger ones are rejected with
+ * ECQ_ERR_WORKSPACE before anything is launched. Nothing is allocated, by
+ * the library or anyone else. The first call on each device looks up the
+ * array's device address (cudaGetSymbolAddress, with that device current);
+ * make that first call before any stream capture. The address is looked up
+ * again when the current CUDA context changes (e.g. after cudaDeviceReset),
+ * and every call clears the matrix's slab counters in the array with a
+ * cudaMemsetAsync on the caller's stream. Every call shares the array: calls whose
  * kernels may overlap on the GPU (other streams, other host threads) race
  * and must be serialised by the caller. Arguments and results are those of
  * ecq_gemv. */

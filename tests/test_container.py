@@ -72,3 +72,41 @@ def test_v1_reference_layout_and_as_written():
     tens = container.read_ecq_v1(path, layout="as_written")
     for name in ("a", "b"):
         assert np.allclose(_oracle_v1(tens[name]), z[f"{name}_dequant"], atol=1e-7)
+
+
+def _bad_offsets(enc, offs):
+    from ecq_b200.codec import EncodedMatrix
+
+    return EncodedMatrix(rows=enc.rows, cols=enc.cols, tile_rows=enc.tile_rows, tile_cols=enc.tile_cols,
+                         table=enc.table, data=enc.data[:96].copy(), tile_offset=np.array(offs, dtype=np.uint32),
+                         stream_len=enc.stream_len)
+
+
+def test_inconsistent_tile_offsets_are_rejected_on_the_host(tmp_path):
+    # 24 x 512 in 8x512 tiles: 3 tiles. Offsets whose largest step is small but
+    # that decrease, or start past 0, or run past a 96-byte blob, would send the
+    # kernels' bulk copies outside the data allocation: they must be refused
+    # before anything is copied to a device (device="cpu" would fail later).
+    from ecq_b200.device import DeviceMatrix
+
+    sym = syn.laplace_symbols(24, 512, b=0.5, seed=4)
+    enc = ecq.encode_matrix(sym, group_size=128)
+    enc.validate()
+    for offs in ([0, 4992, 5008, 96], [32, 64, 96, 96], [0, 64, 32, 96], [0, 32, 64, 128], [0, 40, 64, 96]):
+        bad = _bad_offsets(enc, offs)
+        with pytest.raises(ValueError):
+            bad.validate()
+        with pytest.raises(ValueError):
+            DeviceMatrix.from_encoded(bad, device="cpu")
+    # the same through a v2 file whose offset blob was edited
+    p = tmp_path / "m.ecq"
+    t = container.PackedTensor(enc=enc, scales=syn.group_scales(24, 512, 128, seed=5), group_size=128)
+    container.save_ecq2(p, {"w": t})
+    raw = bytearray(p.read_bytes())
+    good = enc.tile_offset.astype("<u4").tobytes()
+    at = raw.find(good)
+    assert at > 0
+    raw[at:at + len(good)] = np.array([0, 4992, 5008, enc.data.size], dtype="<u4").tobytes()
+    p.write_bytes(bytes(raw))
+    with pytest.raises(ValueError):
+        container.load_ecq2(p)

@@ -32,24 +32,42 @@ def cuda():
         pytest.skip("no CUDA device")
 
 
-def test_noalloc_matches_gemv_on_two_calls():
-    M, K, g = 2056, 4096, 128  # a short last row slab
-    sym = syn.laplace_symbols(M, K, b=0.5, seed=31)
-    sc = torch.from_numpy(syn.group_scales(M, K, g, seed=32)).cuda()
-    x = torch.from_numpy(syn.activations(1, K, seed=33)).cuda()
-    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, group_size=g), group_size=g)
+def _noalloc(m, x, sc):
+    y = torch.full((1, m.rows), float("nan"), dtype=torch.float16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = _lib.lib().ecq_gemv_noalloc(m.view(), _lib.ptr(x), _lib.ptr(sc), _lib.ptr(y), 1, _lib.ptr(status),
+                                     torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, _lib.ERRORS.get(rc, rc)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    return y
+
+
+def _case(M, K, g, seed, tile_cols=None):
+    sym = syn.laplace_symbols(M, K, b=0.5, seed=seed)
+    sc = torch.from_numpy(syn.group_scales(M, K, g, seed=seed + 1)).cuda()
+    x = torch.from_numpy(syn.activations(1, K, seed=seed + 2)).cuda()
+    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, tile_cols=tile_cols, group_size=g), group_size=g)
     y_ref = m.gemv(x, sc)  # ecq_gemv with the matrix's own workspace
     m.check()
-    L = _lib.lib()
-    stream = torch.cuda.current_stream().cuda_stream
+    return m, x, sc, y_ref.reshape(1, M)
+
+
+def test_noalloc_matches_gemv_on_two_calls():
+    m, x, sc, y_ref = _case(2056, 4096, 128, 31)  # a short last row slab
     for _ in range(2):
-        y = torch.full((1, M), float("nan"), dtype=torch.float16, device="cuda")
-        status = torch.zeros(1, dtype=torch.int32, device="cuda")
-        rc = L.ecq_gemv_noalloc(m.view(), _lib.ptr(x), _lib.ptr(sc), _lib.ptr(y), 1, _lib.ptr(status), stream)
-        assert rc == 0, _lib.ERRORS.get(rc, rc)
-        torch.cuda.synchronize()
-        assert int(status.item()) == 0
-        assert _rel_err(y, y_ref.reshape(1, M)) <= RTOL
+        assert _rel_err(_noalloc(m, x, sc), y_ref) <= RTOL
+
+
+def test_noalloc_large_then_small_then_large():
+    # The slab counters follow the per-tile partial sums, so a smaller matrix's
+    # counters fall inside the larger one's partial sums: each call must clear
+    # them. 11008 x 4096 in 8x256 tiles (22016 tiles), then 520 x 1024 (130
+    # tiles, a short last slab), then the large one again.
+    big = _case(11008, 4096, 128, 41, tile_cols=256)
+    small = _case(520, 1024, 128, 51)
+    for m, x, sc, y_ref in (big, small, big, small):
+        assert _rel_err(_noalloc(m, x, sc), y_ref) <= RTOL
 
 
 def test_noalloc_rejects_matrices_beyond_its_scratch():
