@@ -19,8 +19,13 @@ figure through the public API with host buffers, and the reference CPU path
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ecq|reference]
 
-With N > 1 (torchrun, one rank per GPU) every rank runs the same sweep on
-its own GPU (weak scaling; the tiles are independent, no collective).
+With N > 1 (torchrun, one rank per GPU) every matrix is column-sharded
+(K-split) over the N GPUs: each rank decodes its share of the columns of
+every matrix and pushes its fp32 partial y to every rank over NVLink peer
+memory; a sum kernel on each rank closes the all-reduce (strong scaling of
+each GEMV; the value is the whole matrices' effective bytes over the time,
+max over ranks). Before timing, the sharded result is checked against the
+oracle (tp_parity), and the 7B decode step's TP-N logits against TP-1.
 """
 from __future__ import annotations
 
@@ -51,7 +56,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ecq", "reference"], default="ecq")
-    ap.add_argument("--replicas", type=int, default=8)
+    ap.add_argument("--replicas", type=int, default=0,
+                    help="replica sets of the three matrices (0: 8 on one GPU, 5 per GPU on several)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-llama", action="store_true", help="skip the 7B tensor-parallel decode step")
@@ -59,6 +65,7 @@ def parse():
     ap.add_argument("--no-batched", action="store_true", help="skip the 70B-MLP batched-token config")
     ap.add_argument("--no-sweep", action="store_true", help="skip the 8192x8192 entropy sweep")
     ap.add_argument("--no-sharded", action="store_true", help="skip the column-sharded sweep (N > 1)")
+    ap.add_argument("--no-control", action="store_true", help="skip the plain 4-bit GEMV control")
     return ap.parse_args()
 
 
@@ -74,6 +81,37 @@ def make_inputs():
         x = syn.activations(1, K, seed=10 * i + 2)
         enc = ecq.encode_matrix(sym, group_size=GROUP)
         out.append(dict(M=M, K=K, sym=sym, scales=sc, x=x, enc=enc))
+    return out
+
+
+class OracleEncoded:
+    """A packed matrix encoded by the oracle's C restatement of the reference
+    encoder (the fields cpu_baseline reads): the reference arm encodes its
+    inputs this way, so it runs without libecq."""
+
+    def __init__(self, sym, tile_cols):
+        from oracle import oracle
+
+        freq, _ = oracle.table_for(np.bincount(sym.reshape(-1), minlength=16))
+        tiles = oracle.encode_matrix_tiles(sym, freq, 8, tile_cols)
+        self.tile_cols = tile_cols
+        self.table = type("Table", (), {"freq": freq})()
+        self.data = np.concatenate([t[0] for t in tiles])
+        self.tile_offset = np.zeros(len(tiles) + 1, dtype=np.uint32)
+        self.tile_offset[1:] = np.cumsum([t[0].size for t in tiles])
+        self.stream_len = np.concatenate([t[1] for t in tiles]).astype(np.uint16)
+
+
+def make_reference_inputs():
+    """make_inputs' symbols, scales and x, encoded by the oracle (8x512 tiles
+    for K = 4096, 8x256 for K = 11008, as the GPU arm's encoding)."""
+    from ecq_b200 import synthetic as syn
+
+    out = []
+    for i, (M, K) in enumerate(SHAPES):
+        sym = syn.laplace_symbols(M, K, b=LAPLACE_B, seed=10 * i)
+        out.append(dict(M=M, K=K, sym=sym, scales=syn.group_scales(M, K, GROUP, seed=10 * i + 1),
+                        x=syn.activations(1, K, seed=10 * i + 2), enc=OracleEncoded(sym, 512 if K % 512 == 0 else 256)))
     return out
 
 
@@ -187,7 +225,7 @@ def run_reference(args):
         return
     from oracle import oracle
 
-    inputs = make_inputs()
+    inputs = make_reference_inputs()
     threads = oracle.cpu_count()
     eff = sum(d["M"] * d["K"] / 2 for d in inputs)
     # each step: the full sweep once (bounded: ~0.2-1 s on a many-core host)
@@ -201,7 +239,7 @@ def run_reference(args):
     line = {
         "impl": "reference", "metric": "fused decode+GEMV effective 4-bit weight GB/s", "value": round(value, 3),
         "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * dt / args.steps, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(1e3 * dt / args.steps, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "u8", "data": "synthetic",
         "config": {"workload": WORKLOAD, "shapes": SHAPES, "laplace_b": LAPLACE_B, "group_size": GROUP,
                    "batch": 1, "replicas": 1},
@@ -213,11 +251,70 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+class Unit:
+    """One GEMV of a step: a whole matrix (one GPU) or this rank's K-split
+    shard of it (several GPUs), its group scales, its slice of x and the full
+    y [1, M] it produces."""
+
+    def __init__(self, i, M, m, sc, x, y, c0, c1, enc):
+        self.i, self.M, self.m, self.sc, self.x, self.y = i, M, m, sc, x, y
+        self.c0, self.c1, self.enc = c0, c1, enc
+
+
+def _shard_cols(K, world, rank):
+    """This rank's group-aligned column range [c0, c1) of a K-split."""
+    from ecq_b200.codec import split_even
+
+    g0, g1 = split_even(K // GROUP, world)[rank]
+    return g0 * GROUP, g1 * GROUP
+
+
+def build_units(inputs, R, dev, world, rank):
+    """R replica sets of the three shapes. One GPU: each matrix whole, in the
+    standard encoding (8x512 / 8x256 tiles). N GPUs: each rank encodes its
+    K-split shard (same symbols, scales and table) with the widest tile that
+    still gives the shard >= 2048 tiles, so a shard keeps the GPU's warps busy
+    (ecq_b200.model.shard_tile_cols)."""
+    import torch
+
+    import ecq_b200 as ecq
+    from ecq_b200.model import shard_tile_cols
+
+    encs = []
+    for d in inputs:
+        if world == 1:
+            encs.append((d["enc"], 0, d["K"]))
+        else:
+            c0, c1 = _shard_cols(d["K"], world, rank)
+            enc = ecq.encode_matrix(np.ascontiguousarray(d["sym"][:, c0:c1]), d["enc"].table,
+                                    tile_cols=shard_tile_cols(d["M"], c1 - c0), group_size=GROUP)
+            encs.append((enc, c0, c1))
+    units = []
+    for _ in range(R):
+        for i, (d, (enc, c0, c1)) in enumerate(zip(inputs, encs)):
+            units.append(Unit(i, d["M"], ecq.DeviceMatrix.from_encoded(enc, group_size=GROUP, device=dev),
+                              torch.from_numpy(np.ascontiguousarray(d["scales"][:, c0 // GROUP:c1 // GROUP])).to(dev),
+                              torch.from_numpy(np.ascontiguousarray(d["x"][:, c0:c1])).to(dev),
+                              torch.empty(1, d["M"], dtype=torch.float16, device=dev), c0, c1, enc))
+    return units
+
+
+def launch(u, xch, x=None, y=None):
+    """One unit: the fused GEMV (one GPU), or this rank's shard GEMV pushing
+    its fp32 partials to every rank followed by the sum consumer (the
+    column-sharded GEMV with its all-reduce fused in)."""
+    x = u.x if x is None else x
+    y = u.y if y is None else y
+    if xch is None:
+        u.m.gemv(x, u.sc, out=y)
+    else:
+        xch.gemv_push(u.m, x, u.sc)
+        xch.sum(u.M, out=y.view(-1))
+
+
 def run_ecq(args):
     import torch
     import torch.distributed as dist
-
-    import ecq_b200 as ecq
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -227,56 +324,70 @@ def run_ecq(args):
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
-
-    inputs = make_inputs()
-    R = args.replicas
-    sets = []
-    for r in range(R):
-        mats = []
-        for d in inputs:
-            m = ecq.DeviceMatrix.from_encoded(d["enc"], group_size=GROUP, device=dev)
-            mats.append(dict(m=m, sc=torch.from_numpy(d["scales"]).to(dev), x=torch.from_numpy(d["x"]).to(dev),
-                             y=torch.empty(1, d["M"], dtype=torch.float16, device=dev)))
-        sets.append(mats)
-    torch.cuda.synchronize()
-
-    # correctness gate before timing: every shape once against the oracle
-    from oracle import oracle
-
-    for d, e in zip(inputs, sets[0]):
-        y = e["m"].gemv(e["x"], e["sc"], out=e["y"])
-        e["m"].check()
-        yr = oracle.dequant_gemv(d["sym"], d["scales"].astype(np.float32), GROUP, d["x"].astype(np.float32))
-        err = float(np.max(np.abs(y.float().cpu().numpy()[0] - yr)) / np.max(np.abs(yr)))
-        assert err <= 2e-3, f"parity gate failed: {err}"
-
-    stream = torch.cuda.Stream(device=dev)
-    # one graph per step (the whole ring) and one graph per launch (for per-kernel timing)
-    step_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        for mats in sets:  # warm the launch path (attributes) before capture
-            for e in mats:
-                e["m"].gemv(e["x"], e["sc"], out=e["y"])
-        stream.synchronize()
-        with torch.cuda.graph(step_graph, stream=stream):
-            for mats in sets:
-                for e in mats:
-                    e["m"].gemv(e["x"], e["sc"], out=e["y"])
-        launch_graphs = []
-        for mats in sets:
-            row = []
-            for e in mats:
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=stream):
-                    e["m"].gemv(e["x"], e["sc"], out=e["y"])
-                row.append(g)
-            launch_graphs.append(row)
-    launches_per_step = 3 * R
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=600))
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
+
+    def max_ranks(v):
+        t = torch.tensor([float(v)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+
+    inputs = make_inputs()
+    R = args.replicas or (8 if world == 1 else 5 * world)
+    xch = None
+    if world > 1:
+        from ecq_b200.comm import PeerExchange
+
+        xch = PeerExchange(n_max=max(d["M"] for d in inputs), device=dev)
+    units = build_units(inputs, R, dev, world, rank)
+    torch.cuda.synchronize()
+
+    # correctness gate before timing: every shape once against the oracle; at
+    # N > 1 this is the column-sharded GEMV (K-split + fused exchange) checked
+    # against the oracle's whole-matrix dequant + matvec on every rank
+    from oracle import oracle
+
+    y_refs = [oracle.dequant_gemv(d["sym"], d["scales"].astype(np.float32), GROUP, d["x"].astype(np.float32))[0]
+              for d in inputs]
+    errs = []
+    for u in units[:3]:
+        launch(u, xch)
+        torch.cuda.synchronize()
+        u.m.check()
+        if xch is not None:
+            xch.check()
+        yr = y_refs[u.i]
+        errs.append(float(np.max(np.abs(u.y.float().cpu().numpy()[0] - yr)) / np.max(np.abs(yr))))
+    gate_err = max_ranks(max(errs))
+    assert gate_err <= 2e-3, f"parity gate failed: {gate_err}"
+    tp_parity = None
+    if world > 1:
+        tp_parity = {"exchange_rel_err": round(gate_err, 6),
+                     "exchange_vs": "oracle fp64 dequant + matvec of each whole sweep matrix, max over shapes and ranks"}
+        tp_parity.update(rmsnorm_parity(inputs[0], units[0], xch, y_refs[0], dev, max_ranks))
+
+    stream = torch.cuda.Stream(device=dev)
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for u in units:  # warm the launch path (attributes) before capture
+            launch(u, xch)
+        stream.synchronize()
+        with torch.cuda.graph(step_graph, stream=stream):
+            for u in units:
+                launch(u, xch)
+    kernels_per_unit = 1 if world == 1 else 2
+    shard_tiles = {f"{d['M']}x{d['K']}": f"8x{u.enc.tile_cols}" for d, u in zip(inputs, units[:3])}
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -295,104 +406,62 @@ def run_ecq(args):
         ev1.synchronize()
     torch.cuda.synchronize()
     barrier()
-    ms = ev0.elapsed_time(ev1)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_ranks(ev0.elapsed_time(ev1))
+    if xch is not None:
+        xch.check()
     eff_per_step = R * sum(d["M"] * d["K"] / 2 for d in inputs)
     sym_per_step = R * sum(d["M"] * d["K"] for d in inputs)
-    value = world * eff_per_step * args.steps / (ms_max / 1e3) / 1e9
+    value = eff_per_step * args.steps / (ms_max / 1e3) / 1e9
+    ms_step = ms_max / args.steps
 
-    # per-launch durations (events around each single-launch graph, same ring order)
-    per_shape_ms = [[] for _ in SHAPES]
-    with torch.cuda.stream(stream):
-        evs = []
-        n_rounds = max(3, min(args.steps // 4, 50))
-        for _ in range(n_rounds):
-            for row in launch_graphs:
-                for i, g in enumerate(row):
+    split = None
+    if world == 1:
+        # per-launch durations: events around one-launch graphs, cycling the ring
+        graphs = []
+        with torch.cuda.stream(stream):
+            for u in units:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    launch(u, None)
+                graphs.append((u.i, g))
+        per_shape_ms = [[] for _ in SHAPES]
+        with torch.cuda.stream(stream):
+            evs = []
+            for _ in range(max(3, min(args.steps // 4, 50))):
+                for i, g in graphs:
                     a = torch.cuda.Event(enable_timing=True)
                     b = torch.cuda.Event(enable_timing=True)
                     a.record(stream)
                     g.replay()
                     b.record(stream)
                     evs.append((i, a, b))
-    stream.synchronize()
-    for i, a, b in evs:
-        per_shape_ms[i].append(a.elapsed_time(b))
-    avg_ms = [statistics.mean(v) for v in per_shape_ms]
-    share = [a * 1 for a in avg_ms]
-    dom = int(np.argmax(share))
-    d = inputs[dom]
-    alg = algorithmic_bytes(d["enc"], d["M"], d["K"])
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except Exception:
-        pass
-    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-    achieved = alg / (avg_ms[dom] / 1e3) / 1e9
-    traffic = None
+        stream.synchronize()
+        for i, a, b in evs:
+            per_shape_ms[i].append(a.elapsed_time(b))
+        kern_ms = [statistics.mean(v) for v in per_shape_ms]
+        del graphs
+    else:
+        split = exchange_split(units, xch, stream, max_ranks)
+        kern_ms = [split[f"{M}x{K}"]["gemv_push_us"] / 1e3 for M, K in SHAPES]
+    dom = int(np.argmax(kern_ms))
+    du = units[dom]
+    alg = algorithmic_bytes(du.enc, du.M, du.c1 - du.c0)
+    if world > 1:  # the shard's partials go to every rank as 8-byte words instead of an fp16 y
+        alg += du.M * (8 * world - 2)
+    achieved = alg / (kern_ms[dom] / 1e3) / 1e9
+    traffic, traffic_src = None, None
     tf = ROOT / "profiles" / "gemv_dram_traffic.json"
-    if tf.exists():
+    if world == 1 and tf.exists():
         try:
-            traffic = json.loads(tf.read_text()).get(f"{d['M']}x{d['K']}")
+            traffic = json.loads(tf.read_text()).get(f"{du.M}x{du.c1 - du.c0}")
+            traffic_src = ("committed ncu capture (profiles/gemv_dram_traffic.json, dram__bytes_read.sum + "
+                           "dram__bytes_write.sum of this shape's launch), not measured in this run")
         except Exception:
             traffic = None
 
-    # end to end through the public API: x from pinned host, fused GEMVs, y back to pinned host
     e2e = None
     if not args.no_e2e:
-        # every GEMV of the step gets its own x and y; all x of a step arrive in
-        # one pinned host->device copy and all y leave in one device->host copy
-        Ks = [d0["K"] for d0 in inputs]
-        Ms = [d0["M"] for d0 in inputs]
-        hx = torch.cat([torch.from_numpy(d0["x"]).reshape(-1) for _ in sets for d0 in inputs]).pin_memory()
-        hy = torch.empty(R * sum(Ms), dtype=torch.float16).pin_memory()
-        dx = torch.empty_like(hx, device=dev)
-        dy = torch.empty_like(hy, device=dev)
-        views, ox, oy = [], 0, 0
-        for si in range(R):
-            for i in range(len(inputs)):
-                views.append((si, i, dx[ox:ox + Ks[i]].view(1, Ks[i]), dy[oy:oy + Ms[i]].view(1, Ms[i])))
-                ox += Ks[i]
-                oy += Ms[i]
-        e2e_graph = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            with torch.cuda.graph(e2e_graph, stream=stream):
-                dx.copy_(hx, non_blocking=True)
-                for si, i, xv, yv in views:
-                    e = sets[si][i]
-                    e["m"].gemv(xv, e["sc"], out=yv)
-                hy.copy_(dy, non_blocking=True)
-        e2e_steps = max(1, args.steps // 2)
-        with torch.cuda.stream(stream):
-            for _ in range(max(args.warmup, 3)):
-                e2e_graph.replay()
-                stream.synchronize()
-            barrier()
-            a = torch.cuda.Event(enable_timing=True)
-            b = torch.cuda.Event(enable_timing=True)
-            t0 = time.perf_counter()
-            a.record(stream)
-            for _ in range(e2e_steps):
-                e2e_graph.replay()
-                stream.synchronize()  # the host reads every step's results
-                _ = float(hy[0])
-            b.record(stream)
-            b.synchronize()
-            wall = time.perf_counter() - t0
-        te = torch.tensor([max(a.elapsed_time(b), wall * 1e3)], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e_ms = float(te.item())
-        h2d = R * sum(2 * d0["K"] for d0 in inputs)
-        d2h = R * sum(2 * d0["M"] for d0 in inputs)
-        e2e = {"value": round(world * eff_per_step * e2e_steps / (e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-               "path": "DeviceMatrix.gemv (libecq C ABI) in a CUDA graph: every GEMV's x in one pinned-host copy, "
-                       "every y back in one; the host reads y after every step"}
+        e2e = run_e2e(units, xch, stream, args, eff_per_step, barrier, max_ranks)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -406,6 +475,10 @@ def run_ecq(args):
                          f"C restatement of interleaved_rans_decode per tile + dequant + matvec, threads over row "
                          f"slabs"}
 
+    control = None
+    if world == 1 and not args.no_control:
+        control = run_plain4_control(inputs, R, stream, kern_ms, value, hbm_peak)
+
     batched = None
     if not args.no_batched:
         batched = run_batched(dev, world, rank, barrier)
@@ -416,69 +489,271 @@ def run_ecq(args):
 
     sharded = None
     if world > 1 and not args.no_sharded:
-        sharded = run_sharded_sweep(inputs, dev, world, rank, barrier,
-                                    {f"{M}x{K}": round(v * 1e3, 2) for (M, K), v in zip(SHAPES, avg_ms)})
+        sharded = run_sharded_sweep(inputs, units, xch, dev, world, rank, barrier, max_ranks)
+        sharded["gemv_push_and_consumer_split_us"] = split
 
+    comp_bytes_step = sum(algorithmic_bytes(u.enc, u.M, u.c1 - u.c0) for u in units)
+    del step_graph
     llama = None
     if not args.no_llama:
-        del step_graph, launch_graphs
-        if not args.no_e2e:
-            del e2e_graph
-        sets.clear()
+        units.clear()
         torch.cuda.empty_cache()
-        llama = run_llama(args, world, rank, local, dev, barrier)
-        step_graph = launch_graphs = None
+        llama = run_llama(args, world, rank, local, dev, barrier, max_ranks)
+        if llama is not None and world > 1:
+            tp_parity = dict(tp_parity or {}, **llama.pop("tp_parity", {}))
 
-    comp_bytes_step = R * sum(algorithmic_bytes(d0["enc"], d0["M"], d0["K"]) for d0 in inputs)
-    ms_step = ms_max / args.steps
     clk = clocks.summary()
     issue = None
-    try:
-        inst = json.loads((ROOT / "profiles" / "gemv_issue.json").read_text()).get("inst_executed")
-        issue = issue_roofline(sym_per_step / (ms_step / 1e3), SHAPES, inst,
-                               torch.cuda.get_device_properties(dev).multi_processor_count,
-                               float(clk.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)))
-    except (OSError, ValueError):
-        issue = None
+    if world == 1:
+        try:
+            inst = json.loads((ROOT / "profiles" / "gemv_issue.json").read_text()).get("inst_executed")
+            issue = issue_roofline(sym_per_step / (ms_step / 1e3), SHAPES, inst,
+                                   torch.cuda.get_device_properties(dev).multi_processor_count,
+                                   float(clk.get("sm_mhz") or peaks.get("sm_max_mhz", 1965.0)))
+            if issue is not None:
+                issue["inst_source"] = ("committed ncu capture (profiles/gemv_issue.json, smsp__inst_executed.sum "
+                                        "per shape), not measured in this run")
+        except (OSError, ValueError):
+            issue = None
+    if world == 1:
+        tiles = "8x512 (K=4096) / 8x256 (K=11008), 32 streams"
+        par = "one GPU, whole matrices"
+    else:
+        tiles = shard_tiles
+        par = (f"K-split column shard over {world} GPUs: each rank decodes its share of every matrix's columns and "
+               f"pushes fp32 partials to every rank over NVLink peer memory, a sum kernel closes the all-reduce")
     line = {
         "metric": "fused decode+GEMV effective 4-bit weight GB/s", "value": round(value, 3), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
         "config": {"workload": WORKLOAD, "shapes": SHAPES, "laplace_b": LAPLACE_B, "group_size": GROUP,
-                   "batch": 1, "tile": "8x512 (K=4096) / 8x256 (K=11008), 32 streams",
-                   "replicas": R,
-                   "l2": (f"inputs larger than L2: {R} replica sets, {comp_bytes_step / 1e6:.0f} MB per step > 126 MB"
-                          if comp_bytes_step > L2_BYTES else
-                          f"inputs fit in L2 ({R} replica sets, {comp_bytes_step / 1e6:.0f} MB per step <= 126 MB): "
-                          f"not a valid HBM measurement, raise --replicas"),
+                   "batch": 1, "tile": tiles, "replicas": R,
+                   "l2": (f"inputs larger than L2: {R} replica sets, {comp_bytes_step / 1e6:.0f} MB per GPU per step "
+                          f"> 126 MB" if comp_bytes_step > L2_BYTES else
+                          f"inputs fit in L2 ({R} replica sets, {comp_bytes_step / 1e6:.0f} MB per GPU per step <= "
+                          f"126 MB): not a valid HBM measurement, raise --replicas"),
                    "bits_per_symbol": [round(d0["enc"].bits_per_symbol, 4) for d0 in inputs],
-                   "parallelism": f"replicas{world}"},
+                   "parallelism": par},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
-                     "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                     "kernel": f"matrix_kernel gemv {d['M']}x{d['K']}",
-                     "avg_launch_us": round(avg_ms[dom] * 1e3, 2), "algorithmic_bytes": alg,
-                     "per_shape_us": {f"{M}x{K}": round(v * 1e3, 2) for (M, K), v in zip(SHAPES, avg_ms)}},
+                     "frac": round(achieved / hbm_peak, 4), "traffic": traffic, "traffic_source": traffic_src,
+                     "kernel": (f"matrix_kernel gemv {du.M}x{du.c1 - du.c0}" if world == 1 else
+                                f"matrix_kernel gemv + push, shard {du.M}x{du.c1 - du.c0}"),
+                     "avg_launch_us": round(kern_ms[dom] * 1e3, 2), "algorithmic_bytes": alg,
+                     "per_shape_us": {f"{M}x{K}": round(v * 1e3, 2) for (M, K), v in zip(SHAPES, kern_ms)}},
         "views": {
             "effective_4bit_gbs": round(value / world, 2),
-            "compressed_gbs": round(comp_bytes_step / (ms_step / 1e3) / 1e9, 2),
+            "compressed_gbs": round(comp_bytes_step * world / (ms_step / 1e3) / 1e9, 2),
             "symbols_per_s": round(sym_per_step / (ms_step / 1e3), 1),
             "plain_4bit_roofline_gbs": hbm_peak,
             "issue_roofline": issue,
+            "plain_4bit_control": control,
         },
         "e2e": e2e,
         "cpu_baseline": cpu,
-        "llama7b_decode": llama,
         "batched_70b_mlp": batched,
         "entropy_sweep_8192": sweep,
         "column_sharded_sweep": sharded,
-        "gpu_launches": launches_per_step * args.steps,
+        "llama7b_decode": llama,
+        "tp_parity": tp_parity,
+        "gpu_launches": kernels_per_unit * len(inputs) * R * args.steps,
         "clocks": clk,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if xch is not None:
+        xch.close()
     if world > 1:
-        del step_graph, launch_graphs
         dist.destroy_process_group()
+
+
+def rmsnorm_parity(d, u, xch, y_ref, dev, max_ranks):
+    """The row-parallel exchange with its residual add + RMSNorm consumer
+    (gemv push -> ecq_tp_add_rmsnorm_f16) on one sweep shape, against the
+    oracle's dequant + matvec followed by a numpy residual add and RMSNorm
+    (fp16 roundings where the kernel rounds). Returns the max relative errors
+    over ranks."""
+    import torch
+
+    M = d["M"]
+    rng = np.random.default_rng(123)
+    h0 = rng.standard_normal(M).astype(np.float16)
+    w = (1.0 + 0.1 * rng.standard_normal(M)).astype(np.float16)
+    h = torch.from_numpy(h0).to(dev)
+    wt = torch.from_numpy(w).to(dev)
+    xch.gemv_push(u.m, u.x, u.sc)
+    y = xch.add_rmsnorm(h, wt, 1e-5)
+    torch.cuda.synchronize()
+    u.m.check()
+    xch.check()
+    h_ref = (h0.astype(np.float32) + y_ref.astype(np.float16).astype(np.float32)).astype(np.float16)
+    hf = h_ref.astype(np.float32)
+    y_ref2 = (hf / np.sqrt(np.mean(hf * hf) + 1e-5)).astype(np.float16).astype(np.float32) * w.astype(np.float32)
+    eh = float(np.max(np.abs(h.float().cpu().numpy() - hf)) / np.max(np.abs(hf)))
+    ey = float(np.max(np.abs(y.float().cpu().numpy() - y_ref2)) / np.max(np.abs(y_ref2)))
+    return {"residual_rel_err": round(max_ranks(eh), 6), "rmsnorm_rel_err": round(max_ranks(ey), 6),
+            "rmsnorm_shape": f"{M}x{d['K']}"}
+
+
+def exchange_split(units, xch, stream, max_ranks):
+    """Device time of the two kernels of each column-sharded GEMV: the shard
+    GEMV with its push, and the sum consumer (which includes waiting for the
+    slowest rank's push). CUDA events between the launches of an eager run
+    over the whole ring, queued behind a device-side sleep so that host
+    launch gaps do not enter the intervals; median per shape, max over ranks."""
+    import torch
+
+    torch.cuda.synchronize()
+    marks = []
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(50_000_000)
+        for u in units:
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(stream)
+            xch.gemv_push(u.m, u.x, u.sc)
+            e1.record(stream)
+            xch.sum(u.M, out=u.y.view(-1))
+            e2.record(stream)
+            marks.append((u.i, e0, e1, e2))
+    stream.synchronize()
+    xch.check()
+    out = {}
+    for i, (M, K) in enumerate(SHAPES):
+        g = [a.elapsed_time(b) * 1e3 for j, a, b, _ in marks if j == i]
+        c = [b.elapsed_time(e) * 1e3 for j, _, b, e in marks if j == i]
+        out[f"{M}x{K}"] = {"gemv_push_us": round(max_ranks(statistics.median(g)), 2),
+                           "consumer_us": round(max_ranks(statistics.median(c)), 2)}
+    return out
+
+
+def run_e2e(units, xch, stream, args, eff_per_step, barrier, max_ranks):
+    """The same step through the public API with host buffers: every unit's x
+    (this rank's slice) arrives in one pinned host->device copy and every y
+    leaves in one device->host copy, inside the timed region; the host reads y
+    after every step. Max over ranks."""
+    import torch
+
+    dev = units[0].y.device
+    hx = torch.cat([u.x.reshape(-1).cpu() for u in units]).pin_memory()
+    hy = torch.empty(sum(u.M for u in units), dtype=torch.float16).pin_memory()
+    dx = torch.empty_like(hx, device=dev)
+    dy = torch.empty_like(hy, device=dev)
+    views, ox, oy = [], 0, 0
+    for u in units:
+        kx = u.x.numel()
+        views.append((u, dx[ox:ox + kx].view(1, kx), dy[oy:oy + u.M].view(1, u.M)))
+        ox += kx
+        oy += u.M
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            dx.copy_(hx, non_blocking=True)
+            for u, xv, yv in views:
+                launch(u, xch, xv, yv)
+            hy.copy_(dy, non_blocking=True)
+    steps = max(1, args.steps // 2)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            g.replay()
+            stream.synchronize()
+        barrier()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        a.record(stream)
+        for _ in range(steps):
+            g.replay()
+            stream.synchronize()  # the host reads every step's results
+            _ = float(hy[0])
+        b.record(stream)
+        b.synchronize()
+        wall = time.perf_counter() - t0
+    e_ms = max_ranks(max(a.elapsed_time(b), wall * 1e3))
+    del g
+    return {"value": round(eff_per_step * steps / (e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
+            "h2d_bytes_per_step": int(hx.numel() * 2), "d2h_bytes_per_step": int(hy.numel() * 2),
+            "path": "DeviceMatrix.gemv / PeerExchange (libecq C ABI) in a CUDA graph: every GEMV's x in one "
+                    "pinned-host copy, every y back in one; the host reads y after every step"}
+
+
+def run_plain4_control(inputs, R, stream, rans_ms, rans_eff_gbs, hbm_peak):
+    """The in-run control: the same three shapes, scales and x with the
+    symbols stored as plain packed 4-bit (no entropy coding), multiplied by
+    the hand-written plain 4-bit GEMV (ecq_plain4_gemv). R replica sets keep
+    the weights out of L2 exactly as for the rANS sweep; one step is the
+    sweep over all of them in one CUDA graph, timed with CUDA events over 20
+    replays after 3 warm-up replays, plus per-launch times from one-launch
+    graphs cycling over the ring. Returns effective 4-bit GB/s, the HBM fraction of the bytes it
+    moves (weights + scales + x + y) and the rANS/plain time ratio."""
+    import torch
+
+    from ecq_b200.device import Packed4Matrix
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    sets = []
+    for _ in range(R):
+        row = []
+        for d in inputs:
+            row.append(dict(p=Packed4Matrix.from_symbols(d["sym"], GROUP, device=dev),
+                            sc=torch.from_numpy(d["scales"]).to(dev), x=torch.from_numpy(d["x"]).to(dev),
+                            y=torch.empty(1, d["M"], dtype=torch.float16, device=dev)))
+        sets.append(row)
+    from oracle import oracle
+
+    for d, e in zip(inputs, sets[0]):
+        y = e["p"].gemv(e["x"], e["sc"], out=e["y"])
+        yr = oracle.dequant_gemv(d["sym"], d["scales"].astype(np.float32), GROUP, d["x"].astype(np.float32))
+        err = float(np.max(np.abs(y.float().cpu().numpy()[0] - yr)) / np.max(np.abs(yr)))
+        assert err <= 2e-3, f"plain 4-bit parity gate failed: {err}"
+    g = torch.cuda.CUDAGraph()
+    singles = []
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            for row in sets:
+                for e in row:
+                    e["p"].gemv(e["x"], e["sc"], out=e["y"])
+        for row in sets:  # one-launch graphs over the whole ring, so no launch finds its weights in L2
+            for i, e in enumerate(row):
+                gg = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gg, stream=stream):
+                    e["p"].gemv(e["x"], e["sc"], out=e["y"])
+                singles.append((i, gg))
+        for _ in range(3):
+            g.replay()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        steps = 20
+        a.record(stream)
+        for _ in range(steps):
+            g.replay()
+        b.record(stream)
+        b.synchronize()
+        ms = a.elapsed_time(b) / steps
+        per = [[] for _ in inputs]
+        evs = []
+        for _ in range(10):
+            for i, gg in singles:
+                x0 = torch.cuda.Event(enable_timing=True)
+                x1 = torch.cuda.Event(enable_timing=True)
+                x0.record(stream)
+                gg.replay()
+                x1.record(stream)
+                evs.append((i, x0, x1))
+        stream.synchronize()
+    for i, x0, x1 in evs:
+        per[i].append(x0.elapsed_time(x1))
+    per_us = [statistics.median(v) * 1e3 for v in per]
+    eff = R * sum(d["M"] * d["K"] / 2 for d in inputs)
+    moved = R * sum(d["M"] * d["K"] / 2 + 2 * d["M"] * ((d["K"] + GROUP - 1) // GROUP) + 2 * d["K"] + 2 * d["M"]
+                    for d in inputs)
+    eff_gbs = eff / (ms / 1e3) / 1e9
+    del g, singles
+    return {"kernel": "plain4_gemv_kernel (ecq_plain4_gemv), packed nibbles + group-128 fp16 scales",
+            "effective_4bit_gbs": round(eff_gbs, 2),
+            "hbm_gbs": round(moved / (ms / 1e3) / 1e9, 2), "hbm_frac": round(moved / (ms / 1e3) / 1e9 / hbm_peak, 4),
+            "ms_per_sweep": round(ms, 4), "replicas": R,
+            "per_shape_us": {f"{d['M']}x{d['K']}": round(u, 2) for d, u in zip(inputs, per_us)},
+            "rans_over_plain_time": round(eff_gbs / rans_eff_gbs, 3) if rans_eff_gbs else None,
+            "rans_per_shape_us": {f"{d['M']}x{d['K']}": round(v * 1e3, 2) for d, v in zip(inputs, rans_ms)}}
 
 
 def _median_ms(fn, flush, reps=10, warm=3, barrier=None):
@@ -585,81 +860,55 @@ def run_batched(dev, world=1, rank=0, barrier=None):
     return out
 
 
-def run_sharded_sweep(inputs, dev, world, rank, barrier, per_shape_us):
-    """The sweep's three shapes split over the ranks, each whole matrix once
-    per call: K-split (every rank a share of the K-tiles) summed over the
-    ranks by the fused peer exchange (GEMV push + sum kernel) and, for
-    comparison, by an NCCL all-reduce; and row-split (every rank a share of
-    the row slabs) followed by an NCCL all-gather. CUDA events, max over
-    ranks, median of 10 calls each preceded by a 256 MB L2 flush. The fused
-    K-split result is checked against the unsharded GEMV first."""
+def run_sharded_sweep(inputs, units, xch, dev, world, rank, barrier, max_ranks):
+    """Each sweep shape split over the ranks, one whole matrix per call (median
+    of 10 calls, each after a 256 MB L2 flush and a barrier; CUDA events, max
+    over ranks): the K-split shard GEMV closed by the fused peer exchange (the
+    headline's unit), the same shard GEMV closed by an NCCL all-reduce, and a
+    row split (every rank a share of the row slabs, whole K, standard
+    encoding) followed by an NCCL all-gather."""
     import torch
     import torch.distributed as dist
 
     import ecq_b200 as ecq
     from ecq_b200.codec import slice_matrix, split_even
-    from ecq_b200.comm import PeerExchange
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    xch = PeerExchange(n_max=max(d["M"] for d in inputs), device=dev)
     out = {}
+    for d, u in zip(inputs, units[:3]):
+        M, K = d["M"], d["K"]
+        enc = d["enc"]
+        ns, nk = (M + 7) // 8, K // enc.tile_cols
+        s0, s1 = split_even(ns, world)[rank]
+        mr = ecq.DeviceMatrix.from_encoded(slice_matrix(enc, s0, s1, 0, nk), group_size=GROUP, device=dev)
+        sr = torch.from_numpy(np.ascontiguousarray(d["scales"][s0 * 8:min(s1 * 8, M)])).to(dev)
+        x = torch.from_numpy(d["x"]).to(dev)
+        rows_max = max(min(hi * 8, M) - lo * 8 for lo, hi in split_even(ns, world))
+        yr = torch.zeros(1, rows_max, dtype=torch.float16, device=dev)
+        yg = torch.empty(world, rows_max, dtype=torch.float16, device=dev)
 
-    def timed(fn):
-        ms = _median_ms(fn, flush, barrier=barrier)
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        def fused():
+            launch(u, xch)
 
-    try:
-        for (M, K), d in zip(SHAPES, inputs):
-            enc = d["enc"]
-            nk, ns = K // enc.tile_cols, (M + 7) // 8
-            kt0, kt1 = split_even(nk, world)[rank]
-            s0, s1 = split_even(ns, world)[rank]
-            c0, c1 = kt0 * enc.tile_cols, kt1 * enc.tile_cols
-            mk = ecq.DeviceMatrix.from_encoded(slice_matrix(enc, 0, ns, kt0, kt1), group_size=GROUP, device=dev)
-            sk = torch.from_numpy(np.ascontiguousarray(d["scales"][:, c0 // GROUP:c1 // GROUP])).to(dev)
-            xk = torch.from_numpy(np.ascontiguousarray(d["x"][:, c0:c1])).to(dev)
-            mr = ecq.DeviceMatrix.from_encoded(slice_matrix(enc, s0, s1, 0, nk), group_size=GROUP, device=dev)
-            sr = torch.from_numpy(np.ascontiguousarray(d["scales"][s0 * 8:min(s1 * 8, M)])).to(dev)
-            x = torch.from_numpy(d["x"]).to(dev)
-            rows_max = max(min(b * 8, M) - a * 8 for a, b in split_even(ns, world))
-            yr = torch.zeros(1, rows_max, dtype=torch.float16, device=dev)
-            yg = torch.empty(world, rows_max, dtype=torch.float16, device=dev)
-            yk = torch.empty(M, dtype=torch.float16, device=dev)
+        def nccl():
+            y = u.m.gemv(u.x, u.sc)
+            dist.all_reduce(y)
 
-            def fused():
-                xch.gemv_push(mk, xk, sk)
-                return xch.sum(M, out=yk)
+        def rows():
+            mr.gemv(x, sr, out=yr[:, : mr.rows])
+            dist.all_gather_into_tensor(yg, yr)
 
-            def nccl():
-                y = mk.gemv(xk, sk)
-                dist.all_reduce(y)
-                return y
-
-            def rows():
-                mr.gemv(x, sr, out=yr[:, : mr.rows])
-                dist.all_gather_into_tensor(yg, yr)
-                return yg
-
-            y_full = ecq.DeviceMatrix.from_encoded(enc, group_size=GROUP, device=dev).gemv(
-                x, torch.from_numpy(d["scales"]).to(dev))
-            y_f = fused().clone()
-            torch.cuda.synchronize()
-            xch.check()
-            err = float((y_f.float() - y_full[0].float()).abs().max() / y_full.float().abs().max())
-            assert err <= 2e-3, f"sharded parity gate failed for {M}x{K}: {err}"
-            res = {"k_split_fused_us": round(1e3 * timed(fused), 2), "k_split_nccl_us": round(1e3 * timed(nccl), 2),
-                   "row_split_allgather_us": round(1e3 * timed(rows), 2),
-                   "one_gpu_us": per_shape_us.get(f"{M}x{K}"), "max_rel_err": round(err, 6)}
-            res["effective_4bit_gbs_fused"] = round(M * K / 2 / (res["k_split_fused_us"] / 1e6) / 1e9, 1)
-            out[f"{M}x{K}"] = res
-            mk.check()
-            mr.check()
-    finally:
-        xch.close()
+        res = {"shard_tile": f"8x{u.enc.tile_cols}", "shard_bits_per_symbol": round(u.enc.bits_per_symbol, 4),
+               "k_split_fused_us": round(1e3 * max_ranks(_median_ms(fused, flush, barrier=barrier)), 2),
+               "k_split_nccl_us": round(1e3 * max_ranks(_median_ms(nccl, flush, barrier=barrier)), 2),
+               "row_split_allgather_us": round(1e3 * max_ranks(_median_ms(rows, flush, barrier=barrier)), 2)}
+        res["effective_4bit_gbs_fused"] = round(M * K / 2 / (res["k_split_fused_us"] / 1e6) / 1e9, 1)
+        out[f"{M}x{K}"] = res
+        u.m.check()
+        mr.check()
+        xch.check()
     return {"n_gpus": world, "shapes": out,
-            "split": "K-tiles (fused exchange or NCCL all-reduce) / row slabs (NCCL all-gather)"}
+            "split": "K-split shards (fused exchange or NCCL all-reduce) / row slabs (NCCL all-gather)"}
 
 
 def run_entropy_sweep(dev):
@@ -703,14 +952,16 @@ def run_entropy_sweep(dev):
     return {"shape": [M, K], "batch": 1, "cases": rows}
 
 
-def run_llama(args, world, rank, local, dev, barrier):
+def run_llama(args, world, rank, local, dev, barrier, max_ranks):
     """Synthetic Llama-7B batch-1 decode step, tensor-parallel over the ranks,
     captured in one CUDA graph. With several ranks the row-parallel layers'
     all-reduces run fused into the GEMV and the next add + RMSNorm over NVLink
     peer memory; the same weights are also timed with NCCL all-reduces
-    (`tokens_per_s_nccl`). Returns the summary."""
+    (`tokens_per_s_nccl`). Also: the step's device time split by kernel kind
+    (rank 0, one eager step), and at N > 1 the TP-N logits against a TP-1
+    decoder of the same weights and KV cache built on rank 0 (tp_parity).
+    Returns the summary."""
     import torch
-    import torch.distributed as dist
 
     from ecq_b200.model import Llama7BDecoder
 
@@ -743,20 +994,21 @@ def run_llama(args, world, rank, local, dev, barrier):
                 g.replay()
             b.record(s)
         b.synchronize()
-        ms = a.elapsed_time(b) / args.llama_steps
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = max_ranks(a.elapsed_time(b) / args.llama_steps)
         dec.check()
         nxt = int(out.item())
         del g
-        return float(t.item()), nxt
+        return ms, nxt
 
     ms, nxt = timed(True)
+    with torch.cuda.stream(s):
+        breakdown = dec.step_breakdown(tok)
+        logits = dec.step_logits(tok).float().cpu()
     res = {"tokens_per_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 3), "tp": world,
            "exchange": "fused peer-memory all-reduce (GEMV push + add/RMSNorm sum)" if world > 1 else "none",
            "steps": args.llama_steps, "symbols_per_token_per_rank": dec.symbols,
            "compressed_bytes_per_rank": dec.compressed_bytes, "build_s": round(build_s, 1), "next_token": nxt,
+           "breakdown_us_rank0": breakdown,
            "config": "32 layers, hidden 4096, 32 heads x 128, MLP 11008, vocab 32000, 2048-token fp16 KV cache; "
                      "Student-t(4)*0.02 weights, group-128 symmetric 4-bit, rANS per matrix; batch 1; CUDA graph"}
     if world > 1:
@@ -765,6 +1017,25 @@ def run_llama(args, world, rank, local, dev, barrier):
         res["ms_per_token_nccl"] = round(ms_n, 3)
         res["next_token_nccl"] = nxt_n
     dec.close()
+    del dec
+    torch.cuda.empty_cache()
+    if world > 1:
+        par = {}
+        if rank == 0:
+            ref = Llama7BDecoder(tp=1, rank=0, device=dev)
+            with torch.cuda.stream(s):
+                l1 = ref.step_logits(tok).float().cpu()
+            s.synchronize()
+            ref.check()
+            par = {"logits_rel_err_vs_tp1": round(float((logits - l1).abs().max() / l1.abs().max()), 6),
+                   "same_next_token": bool(int(torch.argmax(logits)) == int(torch.argmax(l1)) == nxt),
+                   "next_token_tp1": int(torch.argmax(l1)),
+                   "logits_vs": "TP-1 decoder of the same weights and KV cache on rank 0 (its own exchange-free "
+                                "path), 7B config"}
+            del ref
+            torch.cuda.empty_cache()
+        barrier()
+        res["tp_parity"] = par
     return res
 
 

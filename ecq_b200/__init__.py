@@ -7,6 +7,7 @@ Host-side codec:   RANSTable, InterleavedEncodedTile, interleaved_rans_encode,
 GPU decode:        interleaved_rans_decode, InterleavedRANSDecoder,
                    CudaInterleavedRANS, DeviceMatrix.decode
 Fused GEMV:        DeviceMatrix.gemv, entropy_coded_matmul, EntropyCodedLinear
+Plain 4-bit:       Packed4Matrix (the CACHED store and the HBM-bound control)
 """
 from .codec import (EncodedMatrix, InterleavedEncodedTile, InterleavedRANSEncoder, RANSTable,  # noqa: F401
                     encode_matrix, interleaved_rans_encode, pack_reference_tiles, choose_tile_cols)
@@ -18,7 +19,7 @@ RANS_BYTE_L = 1 << 23
 
 def __getattr__(name):
     # GPU-side modules import torch; load them on first use
-    if name in ("DeviceMatrix", "device_info"):
+    if name in ("DeviceMatrix", "Packed4Matrix", "device_info"):
         from . import device
         return getattr(device, name)
     if name in ("interleaved_rans_decode", "InterleavedRANSDecoder", "CudaInterleavedRANS",

@@ -44,10 +44,12 @@ EXPORTS = (
     "ecq_encode_matrix_host",
     "ecq_decode_interleaved",
     "ecq_matrix_decode",
+    "ecq_matrix_decode_packed4",
     "ecq_matrix_dequantize",
     "ecq_gemv_workspace_bytes",
     "ecq_gemv",
     "ecq_gemv_noalloc",
+    "ecq_plain4_gemv",
     "ecq_matmul_workspace_bytes",
     "ecq_matmul",
     "ecq_device_info",
@@ -106,7 +108,9 @@ def _declare(L: ctypes.CDLL) -> None:
         "ecq_encode_matrix_host": (c_int32, [P, c_uint32, c_uint32, c_uint32, c_uint32, P, c_int32, P, c_int64, P, P, P]),
         "ecq_decode_interleaved": (c_int32, [P, P, c_uint32, c_uint64, c_uint32, P, c_uint32, P, P, P]),
         "ecq_matrix_decode": (c_int32, [POINTER(MatrixView), P, P, P]),
+        "ecq_matrix_decode_packed4": (c_int32, [POINTER(MatrixView), P, P, P]),
         "ecq_matrix_dequantize": (c_int32, [POINTER(MatrixView), P, P, P, P]),
+        "ecq_plain4_gemv": (c_int32, [P, P, P, P, c_uint32, c_uint32, c_uint32, c_uint32, P]),
         "ecq_gemv_workspace_bytes": (c_int64, [POINTER(MatrixView), c_uint32]),
         "ecq_gemv": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, c_int64, P, P]),
         "ecq_gemv_noalloc": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, P]),

@@ -112,6 +112,7 @@ struct MatrixParams {
 constexpr int kModeSymbols = 0;  // store uint8 symbols
 constexpr int kModeGemv = 1;     // fused dequant + GEMV
 constexpr int kModeWeights = 2;  // store dequantised fp16 weights
+constexpr int kModePacked4 = 3;  // store symbols as packed nibbles (column 2i low, 2i+1 high)
 // Reduce v[0..7] over the 32 lanes; lane l ends with the total of row
 // 4*bit4(l) + 2*bit3(l) + bit2(l). Fixed order, so results are deterministic.
 __device__ __forceinline__ float transpose_reduce8(float (&v)[8], int lane) {
@@ -244,7 +245,7 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
     const uint32_t cent = ((p.flags >> ECQ_FLAG_CONSTANT_SYM_SHIFT) & 15u) << 14;  // constant table: sym field
 
     constexpr bool GEMV = MODE == kModeGemv;
-    constexpr bool SCALED = MODE != kModeSymbols;  // needs the group scales
+    constexpr bool SCALED = MODE == kModeGemv || MODE == kModeWeights;  // needs the group scales
     float xs[MPL];  // x * 2^-14 (exact), this lane's columns of the tile
     float acc[kTileRows];
     // Every group scale of the tile, loaded once up front (one load per lane
@@ -326,6 +327,11 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
                     } else if constexpr (MODE == kModeWeights) {
                         // (sym - 8) * 2^14 exactly, times scale * 2^-14: one rounding to fp16
                         p.w_out[idx] = __float2half_rn(entry_weight(e) * gscale);
+                    } else if constexpr (MODE == kModePacked4) {
+                        // lanes 2i and 2i+1 hold columns 2i and 2i+1 (idx is even on even lanes)
+                        const uint32_t sv = (e >> 14) & 15u;
+                        const uint32_t hi = __shfl_down_sync(0xffffffffu, sv, 1);
+                        if (!(lane & 1)) p.sym_out[idx >> 1] = static_cast<uint8_t>(sv | (hi << 4));
                     } else {
                         p.sym_out[idx] = static_cast<uint8_t>((e >> 14) & 15u);
                     }
@@ -464,7 +470,7 @@ struct LaunchShape {
 };
 
 // groups: the kernel applies group scales (GEMV or fp16 weights); stage_x: GEMV
-int32_t shape_for(const ecq_matrix_view* m, bool groups, bool stage_x, LaunchShape* ls) {
+int32_t shape_for(const ecq_matrix_view* m, bool groups, bool stage_x, LaunchShape* ls, bool packed = false) {
     const bool gemv = groups;
     if (!m) return ECQ_ERR_ARG;
     if (m->tile_rows != kTileRows) return ECQ_ERR_UNSUPPORTED;
@@ -482,7 +488,8 @@ int32_t shape_for(const ecq_matrix_view* m, bool groups, bool stage_x, LaunchSha
         }
     }
     if (!(stage_x ? pick_kernel<kModeGemv>(mpl, gpl)
-                  : (groups ? pick_kernel<kModeWeights>(mpl, gpl) : pick_kernel<kModeSymbols>(mpl, gpl))))
+                  : (groups ? pick_kernel<kModeWeights>(mpl, gpl)
+                            : (packed ? pick_kernel<kModePacked4>(mpl, gpl) : pick_kernel<kModeSymbols>(mpl, gpl)))))
         return ECQ_ERR_UNSUPPORTED;
     const uint32_t slabs = (m->rows + kTileRows - 1) / kTileRows;
     if (m->n_tiles != slabs * (m->cols / m->tile_cols)) return ECQ_ERR_SHAPE;
@@ -509,9 +516,9 @@ int32_t shape_for(const ecq_matrix_view* m, bool groups, bool stage_x, LaunchSha
 
 int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, const __half* scales, __half* y,
                       uint8_t* sym_out, void* workspace, uint32_t* status, cudaStream_t stream,
-                      __half* w_out = nullptr, const ecq_tp_comm* comm = nullptr) {
+                      __half* w_out = nullptr, const ecq_tp_comm* comm = nullptr, bool packed = false) {
     LaunchShape ls;
-    int32_t rc = shape_for(m, gemv || w_out != nullptr, gemv, &ls);
+    int32_t rc = shape_for(m, gemv || w_out != nullptr, gemv, &ls, packed);
     if (rc != ECQ_OK) return rc;
     MatrixParams p{};
     p.data = m->data;
@@ -547,7 +554,9 @@ int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, cons
         for (uint32_t q = 0; q < comm->world; ++q) p.tp_peer[q] = static_cast<uint8_t*>(comm->peers[q]);
     }
     KernelFn fn = gemv ? pick_kernel<kModeGemv>(ls.mpl, ls.gpl)
-                       : (w_out ? pick_kernel<kModeWeights>(ls.mpl, ls.gpl) : pick_kernel<kModeSymbols>(ls.mpl, ls.gpl));
+                       : (w_out ? pick_kernel<kModeWeights>(ls.mpl, ls.gpl)
+                                : (packed ? pick_kernel<kModePacked4>(ls.mpl, ls.gpl)
+                                          : pick_kernel<kModeSymbols>(ls.mpl, ls.gpl)));
     if (!ensure_smem_limit(reinterpret_cast<const void*>(fn), kMaxSmem)) return ECQ_ERR_CUDA;
     if (launch_pdl(fn, dim3(ls.ctas), dim3(ls.warps * 32), ls.smem, stream, p) != cudaSuccess) {
         cudaGetLastError();
@@ -583,6 +592,12 @@ int32_t ecq_matrix_decode(const ecq_matrix_view* m, uint8_t* d_out, uint32_t* d_
     if (!view_ok(m) || !d_out || !d_status) return ECQ_ERR_ARG;
     return launch_matrix(m, false, nullptr, nullptr, nullptr, d_out, nullptr, d_status,
                          static_cast<cudaStream_t>(stream));
+}
+
+int32_t ecq_matrix_decode_packed4(const ecq_matrix_view* m, uint8_t* d_out, uint32_t* d_status, void* stream) {
+    if (!view_ok(m) || !d_out || !d_status) return ECQ_ERR_ARG;
+    return launch_matrix(m, false, nullptr, nullptr, nullptr, d_out, nullptr, d_status,
+                         static_cast<cudaStream_t>(stream), nullptr, nullptr, true);
 }
 
 int32_t ecq_matrix_dequantize(const ecq_matrix_view* m, const void* scales_f16, void* w_out_f16, uint32_t* d_status,

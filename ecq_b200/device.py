@@ -100,6 +100,18 @@ class DeviceMatrix:
         check(lib().ecq_matrix_decode(v, ptr(out), ptr(self.status), _stream_ptr(stream)), "matrix decode")
         return out
 
+    def decode_packed4(self, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Decode to plain packed 4-bit [rows, cols/2] uint8 on the device:
+        column 2i in the low nibble of byte i of its row, 2i+1 in the high."""
+        if out is None:
+            out = torch.empty(self.rows, self.cols // 2, dtype=torch.uint8, device=self.device)
+        _require_cuda(out, "out")
+        if out.numel() * 2 != self.rows * self.cols or out.dtype != torch.uint8:
+            raise ValueError("out must be uint8 [rows, cols/2]")
+        check(lib().ecq_matrix_decode_packed4(self.view(), ptr(out), ptr(self.status), _stream_ptr(stream)),
+              "matrix decode to packed 4-bit")
+        return out
+
     def dequantize(self, scales: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
         """Decode to dequantised fp16 weights [rows, cols] = (sym - 8) * scale."""
         ng = (self.cols + self.group_size - 1) // self.group_size
@@ -200,6 +212,71 @@ class DeviceMatrix:
             raise EcqError("device wait timed out")
         if s:
             raise EcqError(f"device status {s:#x}")
+
+
+@dataclass
+class Packed4Matrix:
+    """A plain (not entropy-coded) 4-bit matrix on the device: q [rows,
+    cols/2] uint8 packed nibbles (column 2i low, 2i+1 high), zero point 8,
+    group scales passed per call. The CACHED strategy's store (decode once
+    with ``DeviceMatrix.decode_packed4``) and the bench's plain-4-bit
+    control; ``gemv`` runs ``ecq_plain4_gemv``."""
+
+    rows: int
+    cols: int
+    group_size: int
+    q: torch.Tensor  # uint8 [rows, cols // 2]
+
+    @classmethod
+    def from_symbols(cls, symbols, group_size: int = 128, device="cuda") -> "Packed4Matrix":
+        """Pack a host [rows, cols] symbol matrix (values < 16)."""
+        sym = np.ascontiguousarray(np.asarray(symbols, dtype=np.uint8))
+        if sym.ndim != 2 or sym.shape[1] % 2:
+            raise ValueError("symbols must be [rows, cols] with even cols")
+        q = (sym[:, 0::2] & 15) | ((sym[:, 1::2] & 15) << 4)
+        return cls(rows=sym.shape[0], cols=sym.shape[1], group_size=int(group_size),
+                   q=torch.from_numpy(np.ascontiguousarray(q)).to(torch.device(device)))
+
+    @classmethod
+    def from_matrix(cls, m: DeviceMatrix, stream=None) -> "Packed4Matrix":
+        """Decode an entropy-coded matrix once (on the GPU) into packed 4-bit."""
+        return cls(rows=m.rows, cols=m.cols, group_size=m.group_size, q=m.decode_packed4(stream=stream))
+
+    @property
+    def nbytes(self) -> int:
+        return int(self.q.numel())
+
+    @property
+    def device(self) -> torch.device:
+        return self.q.device
+
+    def gemv(self, x: torch.Tensor, scales: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """y[b] = (q - 8) * scale @ x[b], x [B, cols] or [cols] fp16 (fp16 y)."""
+        squeeze = x.dim() == 1
+        x2 = x.reshape(-1, self.cols)
+        if x2.dtype != torch.float16:
+            raise ValueError("x must be float16")
+        _require_cuda(x2, "x")
+        if x2.data_ptr() % 16:
+            x2 = x2.clone()
+        _require_cuda(scales, "scales")
+        ng = (self.cols + self.group_size - 1) // self.group_size
+        if scales.dtype != torch.float16 or tuple(scales.shape) != (self.rows, ng):
+            raise ValueError(f"scales must be float16 [{self.rows}, {ng}]")
+        B = x2.shape[0]
+        if out is None:
+            out = torch.empty(B, self.rows, dtype=torch.float16, device=self.device)
+        _require_cuda(out, "out")
+        check(lib().ecq_plain4_gemv(ptr(self.q), ptr(scales), ptr(x2), ptr(out), self.rows, self.cols,
+                                    self.group_size, B, _stream_ptr(stream)), "plain 4-bit gemv")
+        return out[0] if squeeze else out
+
+    def symbols(self) -> torch.Tensor:
+        """Unpacked uint8 [rows, cols] symbols (a device copy)."""
+        out = torch.empty(self.rows, self.cols, dtype=torch.uint8, device=self.device)
+        out[:, 0::2] = self.q & 15
+        out[:, 1::2] = self.q >> 4
+        return out
 
 
 def ctypes_view(m: DeviceMatrix) -> MatrixView:

@@ -192,9 +192,16 @@ class Llama7BDecoder:
         g = torch.Generator(device=self.dev).manual_seed(seed + 1000)
         self.embed = (torch.randn(cfg.vocab, H, generator=g, device=self.dev) * 0.02).to(torch.float16)
         self.norm = torch.ones(H, device=self.dev, dtype=torch.float16)
-        # 2048-token KV cache of random fp16 values (+1 slot for the new token)
+        # 2048-token KV cache of random fp16 values (+1 slot for the new token):
+        # every layer's cache is drawn for all heads and this rank keeps its
+        # heads, so every TP size decodes against the same cache
         shape = (cfg.layers, 2, self.local_heads, cfg.kv_len + 1, D)
-        self.kv = torch.randn(shape, generator=g, device=self.dev, dtype=torch.float16)
+        self.kv = torch.empty(shape, device=self.dev, dtype=torch.float16)
+        h0 = rank * self.local_heads
+        for li in range(cfg.layers):
+            full = torch.randn((2, cfg.heads, cfg.kv_len + 1, D), generator=g, device=self.dev, dtype=torch.float16)
+            self.kv[li].copy_(full[:, h0:h0 + self.local_heads])
+            del full
         pos = cfg.kv_len
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, D, 2, device=self.dev, dtype=torch.float32) / D))
         ang = pos * inv
@@ -203,6 +210,7 @@ class Llama7BDecoder:
         self.vocab_sizes = [min(hi * 8, cfg.vocab) - lo * 8 for lo, hi in split_even((cfg.vocab + 7) // 8, tp)]
         self.logits = torch.empty(tp, max(self.vocab_sizes), device=self.dev, dtype=torch.float16)
         self.xch = None
+        self._marks = None  # CUDA events of a step_breakdown run
         self.use_peer = True  # with an exchange: False runs the NCCL path instead (same weights)
         if self.exchange == "peer":
             from .comm import PeerExchange
@@ -227,6 +235,36 @@ class Llama7BDecoder:
         """One batch-1 decode step: token id (int64 [1], device) -> next token id."""
         return torch.argmax(self.step_logits(token).float()).reshape(1)
 
+    def _mark(self, label: str) -> None:
+        """Close the current timed interval under `label` (breakdown runs only)."""
+        if self._marks is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream(self.dev))
+            self._marks.append((label, ev))
+
+    def step_breakdown(self, token: torch.Tensor, sleep_cycles: int = 20_000_000) -> dict:
+        """Device time of one decode step split by kernel kind: CUDA events
+        between consecutive launches of an eager step. A device-side sleep is
+        queued first, so that the host has queued the whole step before the
+        GPU reaches it and host launch gaps do not enter the intervals.
+        Events between launches also stop consecutive kernels from
+        overlapping their prologues, so the parts add up to a little more
+        than a CUDA-graph step. Returns {kind: microseconds per step}."""
+        torch.cuda.synchronize(self.dev)
+        self._marks = []
+        try:
+            torch.cuda._sleep(int(sleep_cycles))
+            self._mark("start")
+            self.step_logits(token)
+            torch.cuda.synchronize(self.dev)
+            out: dict = {}
+            for (_, a), (label, b) in zip(self._marks[:-1], self._marks[1:]):
+                out[label] = out.get(label, 0.0) + a.elapsed_time(b) * 1e3
+        finally:
+            self._marks = None
+        out["total"] = sum(out.values())
+        return {k: round(v, 1) for k, v in out.items()}
+
     def step_logits(self, token: torch.Tensor) -> torch.Tensor:
         """One batch-1 decode step returning the full fp16 logits [vocab]."""
         cfg = self.cfg
@@ -234,42 +272,72 @@ class Llama7BDecoder:
         L = nh * D
         F = self.mlp_rows[1] - self.mlp_rows[0]
         stream = torch.cuda.current_stream(self.dev).cuda_stream
+        mk = self._mark
         h = self.embed[token].reshape(1, cfg.hidden).clone()
+        mk("embed")
         d = None
         peer = self.xch is not None and self.use_peer
         pending = False  # the residual delta sits in the peer exchange (not in d)
         for li, lw in enumerate(self.layers):
-            a = self.xch.add_rmsnorm(h, lw["ln1"], cfg.eps) if pending else self._add_rms(h, d, lw["ln1"])
+            if pending:
+                a = self.xch.add_rmsnorm(h, lw["ln1"], cfg.eps)
+                mk("exchange consumer: sum + add + rmsnorm")
+            else:
+                a = self._add_rms(h, d, lw["ln1"])
+                mk("add + rmsnorm")
             qkv = lw["qkv"](a)                      # [1, 3L]: q | k | v
+            mk("gemv q|k|v")
             kslot = self.kv[li, 0, :, cfg.kv_len]
             vslot = self.kv[li, 1, :, cfg.kv_len]
             check(lib().ecq_rope_kv_f16(qkv.data_ptr(), qkv[:, L:].data_ptr(), qkv[:, 2 * L:].data_ptr(),
                                         kslot.data_ptr(), vslot.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(),
                                         nh, D, (cfg.kv_len + 1) * D, stream), "rope_kv")
+            mk("rope + kv write")
             q = qkv[:, :L].reshape(1, nh, 1, D)
             att = torch.nn.functional.scaled_dot_product_attention(q, self.kv[li, 0].unsqueeze(0),
                                                                    self.kv[li, 1].unsqueeze(0))
+            mk("attention (sdpa)")
             if peer:
                 self.xch.gemv_push(lw["o"].m, att.reshape(1, L).contiguous(), lw["o"].scales)
+                mk("gemv o + push")
                 a = self.xch.add_rmsnorm(h, lw["ln2"], cfg.eps)
+                mk("exchange consumer: sum + add + rmsnorm")
             else:
-                o = self._all_reduce(lw["o"](att.reshape(1, L)))
+                o = lw["o"](att.reshape(1, L))
+                mk("gemv o")
+                o = self._all_reduce(o)
+                mk("nccl all-reduce")
                 a = self._add_rms(h, o, lw["ln2"])
+                mk("add + rmsnorm")
             gu = lw["gate_up"](a)                   # [1, 2F]: gate | up
+            mk("gemv gate|up")
             m = torch.empty(1, F, device=self.dev, dtype=torch.float16)
             check(lib().ecq_silu_mul_f16(gu.data_ptr(), m.data_ptr(), F, 1, stream), "silu_mul")
+            mk("silu * mul")
             if peer:
                 self.xch.gemv_push(lw["down"].m, m, lw["down"].scales)
+                mk("gemv down + push")
                 pending = True
             else:
-                d = self._all_reduce(lw["down"](m))
-        a = self.xch.add_rmsnorm(h, self.norm, cfg.eps) if pending else self._add_rms(h, d, self.norm)
+                d = lw["down"](m)
+                mk("gemv down")
+                d = self._all_reduce(d)
+                mk("nccl all-reduce")
+        if pending:
+            a = self.xch.add_rmsnorm(h, self.norm, cfg.eps)
+            mk("exchange consumer: sum + add + rmsnorm")
+        else:
+            a = self._add_rms(h, d, self.norm)
+            mk("add + rmsnorm")
         logits = self.lm_head(a).reshape(-1)
+        mk("gemv lm_head")
         if self.tp > 1:
             local = torch.full((self.logits.shape[1],), -65504.0, device=self.dev, dtype=torch.float16)
             local[: logits.numel()].copy_(logits)
             dist.all_gather_into_tensor(self.logits.view(-1), local, group=self.group)
-            return torch.cat([self.logits[i, : self.vocab_sizes[i]] for i in range(self.tp)])
+            out = torch.cat([self.logits[i, : self.vocab_sizes[i]] for i in range(self.tp)])
+            mk("logits all-gather")
+            return out
         return logits
 
     def check(self) -> None:

@@ -18,7 +18,7 @@ import torch
 from . import _lib
 from ._lib import MatrixView, check, lib
 from .codec import RANSTable, encode_matrix
-from .device import DeviceMatrix
+from .device import DeviceMatrix, Packed4Matrix
 from .synthetic import quantize_symmetric_groups
 
 
@@ -151,8 +151,14 @@ class EntropyCodedLinear(torch.nn.Module):
     out-of-tree EntropyCodedLinear, experiments/real_model_test.py:135-181).
 
     decode_mode "fused": every forward runs the fused decode+dequant+GEMV.
-    decode_mode "cached": the symbols are decoded once on the GPU at load and
-    the dequantised fp16 weight is kept (the reference's CACHED strategy)."""
+    decode_mode "cached": the weight is decoded once on the GPU at load into
+    plain packed 4-bit (the reference's CACHED strategy, "store as 4-bit",
+    src/decode_strategies.py:43-73) and each forward runs the plain 4-bit
+    GEMV on it (up to 4 tokens per pass over the weights); batches above
+    `cached_gemv_max_batch` expand the 4-bit weight to fp16 for one
+    tensor-core GEMM instead."""
+
+    cached_gemv_max_batch = 8
 
     def __init__(self, matrix: DeviceMatrix, scales: torch.Tensor, bias: torch.Tensor | None = None,
                  decode_mode: str = "fused"):
@@ -165,12 +171,10 @@ class EntropyCodedLinear(torch.nn.Module):
         self.decode_mode = "cached" if decode_mode == "cached" else "fused"
         self.in_features = matrix.cols
         self.out_features = matrix.rows
-        self._weight = None
+        self._packed = None
         if self.decode_mode == "cached":
-            sym = matrix.decode()
+            self._packed = Packed4Matrix.from_matrix(matrix)
             matrix.check()
-            sc = scales.float().repeat_interleave(matrix.group_size, dim=1)[:, : matrix.cols]
-            self._weight = ((sym.float() - 8.0) * sc).to(torch.float16)
 
     @classmethod
     def from_linear(cls, linear: torch.nn.Linear, n_streams: int = 32, decode_mode: str = "fused",
@@ -197,7 +201,12 @@ class EntropyCodedLinear(torch.nn.Module):
         lead = x.shape[:-1]
         x2 = x.reshape(-1, self.in_features).to(torch.float16)
         if self.decode_mode == "cached":
-            y = x2 @ self._weight.t()
+            if x2.shape[0] <= self.cached_gemv_max_batch:
+                y = self._packed.gemv(x2.contiguous(), self.scales)
+            else:
+                sc = self.scales.float().repeat_interleave(self.matrix.group_size, dim=1)[:, : self.in_features]
+                w = ((self._packed.symbols().float() - 8.0) * sc).to(torch.float16)
+                y = torch.mm(x2, w.t(), out_dtype=torch.float32).to(torch.float16)
         else:
             y = rans_matmul(x2.contiguous(), self.matrix, self.scales)
         if self.bias is not None:

@@ -3,7 +3,10 @@
 libecq's kernels instead of numpy threads or Metal queues.
 
 * FUSED     -- get_weights returns None: the GEMV kernel decodes (ops.py).
-* CACHED    -- load_layer decodes once on the GPU and keeps the symbols.
+* CACHED    -- load_layer decodes once on the GPU and keeps the weights as
+  plain packed 4-bit (DecodeOnceStrategy's "store as 4-bit"); a packed
+  matrix's cached weights multiply with the plain 4-bit GEMV
+  (``DecodedWeights.packed.gemv``).
 * LRU       -- decode on first use, keep within a byte budget, evict LRU.
 * PREFETCH / GPU_ASYNC -- prefetch_layer decodes on a side CUDA stream and
   records an event; get_weights makes the caller's stream wait on it (no
@@ -26,7 +29,7 @@ import numpy as np
 import torch
 
 from .codec import InterleavedEncodedTile
-from .device import DeviceMatrix
+from .device import DeviceMatrix, Packed4Matrix
 
 
 class DecodeMode(Enum):
@@ -39,16 +42,26 @@ class DecodeMode(Enum):
 
 @dataclass
 class DecodedWeights:
-    """src/decode_strategies.py:31-40, with device-resident indices."""
+    """src/decode_strategies.py:31-40, with device-resident weights: either
+    uint8 indices, or (CACHED mode, packed matrices) a ``Packed4Matrix`` whose
+    indices are unpacked only when asked for."""
 
-    indices: torch.Tensor  # uint8 on the device, reshaped to `shape`
+    _indices: Optional[torch.Tensor]  # uint8 on the device, reshaped to `shape`
     scale: Any
     zero_point: Any
     shape: tuple
+    packed: Optional[Packed4Matrix] = None
+
+    @property
+    def indices(self) -> torch.Tensor:
+        if self._indices is None:
+            self._indices = self.packed.symbols().reshape(self.shape)
+        return self._indices
 
     @property
     def nbytes(self) -> int:
-        return int(self.indices.numel())
+        """Bytes the cache holds: 4 bits per weight when packed."""
+        return self.packed.nbytes if self.packed is not None else int(self._indices.numel())
 
     def numpy(self) -> np.ndarray:
         return self.indices.cpu().numpy()
@@ -95,10 +108,16 @@ class SmartDecoder:
         """Decode a layer now (CACHED mode), as DecodeOnceStrategy.load_layer."""
         if self.mode != DecodeMode.CACHED:
             return
-        out, status, _ = _decode_async(tile, shape, torch.cuda.current_stream())
-        self._check(status)
+        if isinstance(tile, DeviceMatrix):
+            pk = Packed4Matrix.from_matrix(tile)
+            self._check(tile.status)
+            dw = DecodedWeights(None, scale, zero_point, tuple(shape) or (tile.rows, tile.cols), packed=pk)
+        else:
+            out, status, _ = _decode_async(tile, shape, torch.cuda.current_stream())
+            self._check(status)
+            dw = DecodedWeights(out, scale, zero_point, tuple(shape) or tuple(out.shape))
         with self.lock:
-            self.cache[name] = DecodedWeights(out, scale, zero_point, tuple(shape) or tuple(out.shape))
+            self.cache[name] = dw
 
     def prefetch_layer(self, name: str, tile, scale=0.0, zero_point=0.0, shape: tuple = ()) -> None:
         """Start decoding on the side stream (PREFETCH / GPU_ASYNC)."""

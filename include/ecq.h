@@ -154,6 +154,13 @@ int32_t ecq_decode_interleaved(const uint8_t *d_data, const uint32_t *d_lengths,
  * parallel_rans_decode_async, src/decode_strategies.py:336-390). */
 int32_t ecq_matrix_decode(const ecq_matrix_view *m, uint8_t *d_out, uint32_t *d_status, void *stream);
 
+/* Decode a packed matrix to plain packed 4-bit, d_out[rows, cols/2] bytes
+ * (column 2i in the low nibble of byte i of its row, column 2i+1 in the
+ * high nibble): the CACHED strategy's 4-bit store (DecodeOnceStrategy,
+ * src/decode_strategies.py:43-73, "store as 4-bit"), consumed by
+ * ecq_plain4_gemv. Symbols are those ecq_matrix_decode returns. */
+int32_t ecq_matrix_decode_packed4(const ecq_matrix_view *m, uint8_t *d_out, uint32_t *d_status, void *stream);
+
 /* Decode a packed matrix straight to dequantised fp16 weights
  * w_out[r, c] = (sym[r,c] - 8) * scales[r, c/g] (row-major [rows, cols]):
  * the batched-token path, which decodes once and hands W to a tensor-core
@@ -210,6 +217,22 @@ int32_t ecq_gemv(const ecq_matrix_view *m, const void *x_f16, const void *scales
  * ecq_gemv. */
 int32_t ecq_gemv_noalloc(const ecq_matrix_view *m, const void *x_f16, const void *scales_f16, void *y_f16,
                          uint32_t batch, uint32_t *d_status, void *stream);
+
+/* ---------------- device: plain 4-bit GEMV ---------------- */
+
+/* y[b, r] = sum_c (q[r, c] - 8) * scales[r, c/g] * x[b, c] for plain packed
+ * 4-bit weights q [rows, cols/2] bytes (layout of ecq_matrix_decode_packed4),
+ * fp16 scales [rows, cols/g], x [batch, cols] fp16, y [batch, rows] fp16:
+ * fp16 products summed 8 at a time, then fp32 with the group scale;
+ * deterministic. Up to 4 tokens share one pass over the weights. Needs
+ * cols % 32 == 0, group_size a power of two >= 32, q and x 16-byte aligned.
+ * Two roles: the CACHED strategy's GEMV after ecq_matrix_decode_packed4
+ * (src/decode_strategies.py:43-73 decodes once, then multiplies), and an
+ * HBM-bound control beside the fused rANS GEMV on the same shapes (the
+ * reference's nibble-LUT kernel fused_memory_bench,
+ * src/metal_interleaved.py:555-683, plays that role on Apple GPUs). */
+int32_t ecq_plain4_gemv(const void *q_packed, const void *scales_f16, const void *x_f16, void *y_f16, uint32_t rows,
+                        uint32_t cols, uint32_t group_size, uint32_t batch, void *stream);
 
 /* ---------------- device: fused decode + dequant + tensor-core GEMM ---------------- */
 

@@ -62,3 +62,37 @@ def test_cpu_baseline_runs_until_its_time_bound(bench):
     assert sweeps >= 2 and secs >= 0.05 and gbs > 0
     gbs1, secs1, sweeps1 = bench.cpu_baseline([d], threads=1, repeats=1)
     assert sweeps1 == 1 and secs1 > 0 and gbs1 > 0
+
+
+def test_reference_arm_encoding_matches_the_library(bench):
+    # the reference arm encodes with the oracle (no libecq); its bytes must be
+    # the library's for the same symbols and table
+    import numpy as np
+
+    import ecq_b200 as ecq
+    from ecq_b200 import synthetic as syn
+
+    sym = syn.laplace_symbols(24, 1024, b=0.5, seed=3)
+    o = bench.OracleEncoded(sym, 512)
+    e = ecq.encode_matrix(sym, group_size=bench.GROUP)
+    assert np.array_equal(o.table.freq, e.table.freq)
+    assert np.array_equal(o.data, e.data)
+    assert np.array_equal(o.tile_offset, e.tile_offset)
+    assert np.array_equal(o.stream_len, e.stream_len)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_k_split_shards_cover_the_columns(bench, world):
+    # every sweep shape's columns split into contiguous, group-aligned shards,
+    # each with a tile width that the kernels support
+    from ecq_b200.model import shard_tile_cols
+
+    for M, K in bench.SHAPES:
+        edges = [bench._shard_cols(K, world, r) for r in range(world)]
+        assert edges[0][0] == 0 and edges[-1][1] == K
+        for (a0, a1), (b0, b1) in zip(edges, edges[1:]):
+            assert a1 == b0
+        for c0, c1 in edges:
+            assert c0 % bench.GROUP == 0 and c1 > c0
+            tc = shard_tile_cols(M, c1 - c0)
+            assert (c1 - c0) % tc == 0 and tc in (128, 256, 512)

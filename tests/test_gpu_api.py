@@ -109,7 +109,8 @@ def test_smart_decoder_modes(mat):
     d.load_layer("m", m, 0.02, -0.16, (m.rows, m.cols))
     assert np.array_equal(d.get_weights("l0").numpy(), sym[:64])
     assert np.array_equal(d.get_weights("m").numpy(), sym)
-    assert d.memory_usage() == sym[:64].size + sym.size
+    assert d.memory_usage() == sym[:64].size + sym.size // 2  # the packed matrix is cached as 4-bit
+    assert d.get_weights("m").packed is not None
 
     d = strategies.SmartDecoder("lru", max_memory_bytes=sym.size + 10)
     assert np.array_equal(d.get_weights("m", m, 1.0, 0.0, (m.rows, m.cols)).numpy(), sym)

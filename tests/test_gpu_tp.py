@@ -41,6 +41,8 @@ def _worker(rank, world, port, which):
     try:
         if which == "exchange":
             _exchange(rank, world, dev)
+        elif which == "exchange_large":
+            _exchange(rank, world, dev, M=11008, n_max=11008)
         else:
             _decoder(rank, world, dev)
     finally:
@@ -49,14 +51,14 @@ def _worker(rank, world, port, which):
         dist.destroy_process_group()
 
 
-def _exchange(rank, world, dev):
+def _exchange(rank, world, dev, M=520, n_max=1024):
     import ecq_b200 as ecq
     from ecq_b200 import synthetic as syn
     from ecq_b200.codec import slice_matrix, split_even
     from ecq_b200.comm import PeerExchange
     from oracle import oracle
 
-    M, K, g = 520, 2048, 128
+    K, g = 2048, 128
     sym = syn.laplace_symbols(M, K, b=0.5, seed=61)
     sc = syn.group_scales(M, K, g, seed=62)
     enc = ecq.encode_matrix(sym, tile_cols=512, group_size=g)
@@ -65,7 +67,7 @@ def _exchange(rank, world, dev):
     c0, c1 = kt0 * 512, kt1 * 512
     s_loc = torch.from_numpy(np.ascontiguousarray(sc[:, c0 // g:c1 // g])).to(dev)
     w = torch.from_numpy((1.0 + 0.1 * np.random.default_rng(63).standard_normal(M)).astype(np.float16)).to(dev)
-    xch = PeerExchange(n_max=1024, device=dev)
+    xch = PeerExchange(n_max=n_max, device=dev)
     try:
         for it in range(5):  # several epochs: both buffer halves, flags re-armed
             x = syn.activations(1, K, seed=70 + it)
@@ -104,10 +106,9 @@ def _decoder(rank, world, dev):
     ref = Llama7BDecoder(cfg, device=dev, tp=1, seed=5)
     l_ref = ref.step_logits(tok).float()
     dec = Llama7BDecoder(cfg, device=dev, tp=world, rank=rank, seed=5, exchange="peer")
-    # the random KV cache is drawn per decoder shape: give this rank the
-    # reference's cache of its heads
+    # every TP size draws the same global KV cache and keeps its heads
     nh = dec.local_heads
-    dec.kv.copy_(ref.kv[:, :, rank * nh:(rank + 1) * nh])
+    assert torch.equal(dec.kv, ref.kv[:, :, rank * nh:(rank + 1) * nh])
     try:
         l_peer = dec.step_logits(tok).float()
         dec.use_peer = False
@@ -136,7 +137,17 @@ def _decoder(rank, world, dev):
         dec.close()
 
 
-@pytest.mark.parametrize("which", ["exchange", "decoder"])
+@pytest.mark.parametrize("which", ["exchange", "exchange_large"])
+def test_peer_exchange_one_rank(which):
+    """One rank pushing to itself: the fused GEMV's push and both multi-CTA
+    consumers (3 CTAs for 520 rows, 32 for 11008) against the oracle over
+    several epochs, on one GPU."""
+    import torch.multiprocessing as mp
+
+    mp.spawn(_worker, args=(1, _free_port(), which), nprocs=1, join=True)
+
+
+@pytest.mark.parametrize("which", ["exchange", "exchange_large", "decoder"])
 def test_peer_exchange_two_gpus(which):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
