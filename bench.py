@@ -789,13 +789,16 @@ def _device_laplace(M, K, b, dev, seed):
 
 
 def run_batched(dev, world=1, rank=0, barrier=None):
-    """70B-MLP-shaped 28672 x 8192 matrix (Laplace b = 0.5, group-128 scales,
-    8x256 tiles) at token batches 1, 8, 32, 128: batch 1 runs the fused GEMV,
-    larger batches the tcgen05 kernel that decodes each tile straight into the
-    tensor core's shared-memory operand (no decoded weight in HBM). As a
-    control, the same encoding decoded to fp16 in HBM + a cuBLAS GEMM. With
-    several ranks the matrix is column-sharded: each rank holds an even share
-    of the K-tiles (same encoding), computes a partial y and an NCCL
+    """70B-MLP-shaped 28672 x 8192 matrix (Laplace b = 0.5, group-128 scales)
+    at token batches 1, 8, 32, 128 through DeviceMatrix.matmul, the one
+    dispatch of the batched entry points: up to 8 tokens the fused GEMV that
+    decodes each tile once for the whole batch, more the tcgen05 kernel that
+    decodes each tile straight into the tensor core's shared-memory operand
+    (8x256 tiles); no decoded weight goes to HBM on either. Also: B = 8 on the
+    standard 8x512 encoding (batched GEMV) and on the tcgen05 kernel, and, as
+    a control, the 8x256 encoding decoded to fp16 in HBM + a cuBLAS GEMM.
+    With several ranks the matrix is column-sharded: each rank holds an even
+    share of the K-tiles (same encoding), computes a partial y and an NCCL
     all-reduce sums them. CUDA events, max over ranks; 3 warm-up and 10 timed
     calls, each preceded by a 256 MB write that flushes L2."""
     import torch
@@ -805,22 +808,27 @@ def run_batched(dev, world=1, rank=0, barrier=None):
     from ecq_b200 import synthetic as syn
     from ecq_b200.codec import slice_matrix, split_even
 
-    M, K, TC = 28672, 8192, 256
+    M, K = 28672, 8192
     sym = _device_laplace(M, K, LAPLACE_B, dev, 0)
-    enc = ecq.encode_matrix(sym, tile_cols=TC, group_size=GROUP)
     sc_all = syn.group_scales(M, K, GROUP, seed=1)
-    nk = K // enc.tile_cols
-    kt0, kt1 = split_even(nk, world)[rank]
-    if world > 1:
-        enc = slice_matrix(enc, 0, (M + 7) // 8, kt0, kt1)
-    c0, c1 = kt0 * enc.tile_cols, kt1 * enc.tile_cols
-    m = ecq.DeviceMatrix.from_encoded(enc, group_size=GROUP, device=dev)
+    mats = {}
+    for TC in (256, 512):
+        enc = ecq.encode_matrix(sym, tile_cols=TC, group_size=GROUP)
+        nk = K // TC
+        # the same column range on both encodings: shards of 512 columns
+        kt0, kt1 = split_even(K // 512, world)[rank]
+        kt0, kt1 = kt0 * (512 // TC), kt1 * (512 // TC)
+        if world > 1:
+            enc = slice_matrix(enc, 0, (M + 7) // 8, kt0, kt1)
+        mats[TC] = (ecq.DeviceMatrix.from_encoded(enc, group_size=GROUP, device=dev), enc, kt0 * TC, kt1 * TC, nk)
+    m, enc, c0, c1, nk = mats[256]
+    m512 = mats[512][0]
     sc = torch.from_numpy(np.ascontiguousarray(sc_all[:, c0 // GROUP:c1 // GROUP])).to(dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     gx = torch.Generator(device=dev).manual_seed(5)
-    out = {"shape": [M, K], "tile": f"8x{TC}", "bits_per_symbol": round(enc.bits_per_symbol, 4), "n_gpus": world,
-           "shard": f"K-tiles [{kt0}, {kt1}) of {nk} per rank" if world > 1 else "whole matrix",
-           "batches": {}}
+    out = {"shape": [M, K], "tile": "8x256 (8x512 where stated)", "bits_per_symbol": round(enc.bits_per_symbol, 4),
+           "bits_per_symbol_8x512": round(mats[512][1].bits_per_symbol, 4), "n_gpus": world,
+           "shard": f"columns [{c0}, {c1}) of {K} per rank" if world > 1 else "whole matrix", "batches": {}}
 
     def timed(fn):
         ms = _median_ms(fn, flush, barrier=barrier)
@@ -830,33 +838,39 @@ def run_batched(dev, world=1, rank=0, barrier=None):
             ms = float(t.item())
         return ms
 
+    def reduce(y):
+        if world > 1:
+            dist.all_reduce(y)
+        return y
+
+    def row_of(B, ms, path):
+        return {"ms": round(ms, 4), "tokens_per_s": round(B * 1000.0 / ms, 1),
+                "effective_4bit_gbs": round(M * K / 2 / (ms / 1e3) / 1e9, 1),
+                "symbols_per_s": round(M * K / (ms / 1e3), 1),
+                "useful_tflops": round(2.0 * B * M * K / (ms / 1e3) / 1e12, 2),
+                "path": path + (" + NCCL all-reduce" if world > 1 else "")}
+
     for B in (1, 8, 32, 128):
         x = torch.randn(B, K, device=dev, dtype=torch.float16, generator=gx)[:, c0:c1].contiguous()
-
-        def fused():
-            y = m.matmul(x, sc)
-            if world > 1:
-                dist.all_reduce(y)
-            return y
-
-        def control():
-            y = torch.mm(x, m.dequantize(sc).t(), out_dtype=torch.float32).to(torch.float16)
-            if world > 1:
-                dist.all_reduce(y)
-            return y
-
-        ms = timed(fused)
-        row = {"ms": round(ms, 4), "tokens_per_s": round(B * 1000.0 / ms, 1),
-               "effective_4bit_gbs": round(M * K / 2 / (ms / 1e3) / 1e9, 1),
-               "symbols_per_s": round(M * K / (ms / 1e3), 1),
-               "useful_tflops": round(2.0 * B * M * K / (ms / 1e3) / 1e12, 2),
-               "path": ("fused GEMV" if B == 1 else "fused decode + tcgen05 MMA (x in TMEM, W tile in SMEM)")
-               + (" + NCCL all-reduce" if world > 1 else "")}
+        m.ensure_workspace(min(B, 8))
+        m512.ensure_workspace(min(B, 8))
+        ms = timed(lambda: reduce(m.matmul(x, sc)))
+        path = ("fused GEMV" if B == 1 else
+                "fused GEMV, each tile decoded once for the 8 tokens" if B <= 8 else
+                "fused decode + tcgen05 MMA (x in TMEM, W tile in SMEM)")
+        row = row_of(B, ms, path + " [8x256 tiles]")
         if B > 1:
-            cms = timed(control)
-            row["control_decode_fp16_cublas_ms"] = round(cms, 4)
+            row["control_decode_fp16_cublas_ms"] = round(
+                timed(lambda: reduce(torch.mm(x, m.dequantize(sc).t(), out_dtype=torch.float32).to(torch.float16))), 4)
+        if B in (1, 8):
+            row["gemv_8x512_ms"] = round(timed(lambda: reduce(m512.gemv(x, sc))), 4)
+        if B == 8:
+            row["tcgen05_ms"] = round(timed(lambda: reduce(m.matmul_tc(x, sc))), 4)
         out["batches"][str(B)] = row
+    b1, b8 = out["batches"]["1"], out["batches"]["8"]
+    out["b8_over_b1_time_8x512"] = round(b8["gemv_8x512_ms"] / b1["gemv_8x512_ms"], 3)
     m.check()
+    m512.check()
     return out
 
 

@@ -93,14 +93,16 @@ struct MatrixParams {
     __half* y;             // [rows]
     uint8_t* sym_out;      // [rows, cols] (decode mode: symbols)
     __half* w_out;         // [rows, cols] (decode mode: dequantised fp16 weights, when set)
-    float* partials;       // [n_tiles, 8]
-    uint32_t* slab_count;  // [n_slabs]
+    float* partials;       // [n_tiles, 8, nb] (GEMV modes)
+    uint32_t* slab_count;  // [n_slabs] (GEMV modes; first in the workspace)
     uint32_t* status;
     uint32_t rows, cols, ng, group_size;
     uint32_t n_ktiles, n_tiles;
     uint32_t buf_bytes;
     uint32_t flags;
     uint32_t x_bytes;  // x staged in shared memory after the table (0: read x from global)
+    uint32_t xs_bytes;  // batched GEMV: x of nb tokens staged as fp16 [cols][nb] after the table
+    uint32_t nb, batch_here;  // batched GEMV: tokens per launch, of which the first batch_here are real
     // tensor-parallel push (ecq_gemv_tp; tp_world == 0 otherwise): y goes as
     // fp32 partials to every rank's exchange buffer instead of to p.y
     uint8_t* tp_peer[ECQ_TP_MAX_RANKS];
@@ -113,6 +115,7 @@ constexpr int kModeSymbols = 0;  // store uint8 symbols
 constexpr int kModeGemv = 1;     // fused dequant + GEMV
 constexpr int kModeWeights = 2;  // store dequantised fp16 weights
 constexpr int kModePacked4 = 3;  // store symbols as packed nibbles (column 2i low, 2i+1 high)
+constexpr int kModeGemvBatch = 4;  // fused dequant + GEMV for NB tokens, each tile decoded once
 // Reduce v[0..7] over the 32 lanes; lane l ends with the total of row
 // 4*bit4(l) + 2*bit3(l) + bit2(l). Fixed order, so results are deterministic.
 __device__ __forceinline__ float transpose_reduce8(float (&v)[8], int lane) {
@@ -354,16 +357,206 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
     if constexpr (GEMV) finish_tile(p, t, acc, rows_here, lane, pend);
 }
 
-// Shared memory: [decode table 64 KB][2 stage buffers per warp][read-ahead pad][mbarriers]
-template <int MPL, int GPL, int MODE>
+// Reduce v[0..N) (N = 2, 4 or 8) over the 32 lanes in a fixed order. Lane l
+// ends with the total of value index (l>>4 & 1)*N/2 + (l>>3 & 1)*N/4 +
+// (l>>2 & 1)*N/8 (the terms that exist for N); the lanes whose bits below
+// log2(N)... are zero hold each index once (see reduce_owner).
+template <int N>
+__device__ __forceinline__ float transpose_reduce(float (&v)[N], int lane) {
+    if constexpr (N == 8) {
+        return transpose_reduce8(v, lane);
+    } else {
+        int w = N;
+#pragma unroll
+        for (int bit = 16; w > 1; bit >>= 1) {
+            const bool hi = lane & bit;
+#pragma unroll
+            for (int i = 0; i < w / 2; ++i) {
+                const float send = hi ? v[i] : v[i + w / 2];
+                const float keep = hi ? v[i + w / 2] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+            }
+            w >>= 1;
+        }
+        constexpr int first_full = N == 4 ? 4 : 8;  // the bit after the halving levels
+#pragma unroll
+        for (int bit = first_full; bit; bit >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], bit);
+        return v[0];
+    }
+}
+// value index transpose_reduce<N> leaves in `lane`, and whether this lane is
+// the one that stores it
+template <int N>
+__device__ __forceinline__ int reduce_index(int lane) {
+    if constexpr (N == 8) return ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+    if constexpr (N == 4) return ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+    return (lane >> 4) & 1;
+}
+template <int N>
+__device__ __forceinline__ bool reduce_owner(int lane) {
+    return (lane & (N == 8 ? 3 : (N == 4 ? 7 : 15))) == 0;
+}
+
+// x of NB tokens for one column, fp16 x 8 (pairs of tokens), from the staged
+// [cols][NB] block
+template <int NB>
+__device__ __forceinline__ void lds_x(uint32_t addr, __half2 (&xh)[NB / 2]) {
+    if constexpr (NB == 8) {
+        uint32_t a, b, c, d;
+        asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "r"(addr));
+        xh[0] = *reinterpret_cast<__half2*>(&a);
+        xh[1] = *reinterpret_cast<__half2*>(&b);
+        xh[2] = *reinterpret_cast<__half2*>(&c);
+        xh[3] = *reinterpret_cast<__half2*>(&d);
+    } else if constexpr (NB == 4) {
+        uint32_t a, b;
+        asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(a), "=r"(b) : "r"(addr));
+        xh[0] = *reinterpret_cast<__half2*>(&a);
+        xh[1] = *reinterpret_cast<__half2*>(&b);
+    } else {
+        uint32_t a;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(a) : "r"(addr));
+        xh[0] = *reinterpret_cast<__half2*>(&a);
+    }
+}
+
+// Batched GEMV: the slab's last tile sums the partials of its 8 rows x NB
+// tokens over the K-tiles in fixed order and writes y[b, row].
+template <int NB>
+__device__ __forceinline__ void complete_pending_batch(const MatrixParams& p, PendingSlab& pend, int lane) {
+    if (pend.slab == 0xffffffffu) return;
+    const uint32_t old = __shfl_sync(0xffffffffu, pend.old, 0);
+    if (old == p.n_ktiles - 1) {
+        __threadfence();
+        const uint32_t slab = pend.slab;
+        const float* base = p.partials + static_cast<size_t>(slab) * p.n_ktiles * kTileRows * NB;
+#pragma unroll
+        for (int v = lane; v < kTileRows * NB; v += 32) {
+            const int row = v / NB, b = v % NB;
+            float s = 0.f;
+            for (uint32_t k = 0; k < p.n_ktiles; ++k) s += __ldcg(base + static_cast<size_t>(k) * kTileRows * NB + v);
+            if (row < pend.rows && b < static_cast<int>(p.batch_here))
+                p.y[static_cast<size_t>(b) * p.rows + slab * kTileRows + row] = __float2half_rn(s);
+        }
+        if (lane == 0) p.slab_count[slab] = 0u;
+    }
+    pend.slab = 0xffffffffu;
+}
+
+// Decode one tile once and accumulate its contribution for NB tokens. Per
+// symbol: the weight (s - 8) / 8 exactly in both halves of an fp16 pair, times
+// the NB tokens' x * 8 (fp16 pairs from shared memory), summed in fp16 over
+// the GPL symbols a lane holds of one scale group, then in fp32 with the
+// group scale; per row, a fixed-order warp reduction of the NB sums.
+template <int MPL, int GPL, int NB, bool CONSTANT>
+__device__ __forceinline__ void process_tile_batch(const MatrixParams& p, uint32_t t, uint32_t buf, uint32_t tb,
+                                                   uint32_t xsb, int lane, PendingSlab& pend) {
+    constexpr int NSG = MPL / GPL;
+    constexpr int NH = NB / 2;
+    const uint32_t slab = t / p.n_ktiles;
+    const uint32_t kt = t - slab * p.n_ktiles;
+    const uint32_t r0 = slab * kTileRows;
+    const int rows_here = static_cast<int>(min(static_cast<uint32_t>(kTileRows), p.rows - r0));
+    const uint32_t c0 = kt * (MPL * 32);
+    const uint32_t len = p.stream_len[t * 32 + lane];
+
+    uint32_t a = buf + lane;
+    uint32_t x = (lds_u8(a) << 24) | (lds_u8(a + 32) << 16) | (lds_u8(a + 64) << 8) | lds_u8(a + 96);
+    a += 128;
+    const uint32_t cent = ((p.flags >> ECQ_FLAG_CONSTANT_SYM_SHIFT) & 15u) << 14;
+
+    constexpr int NSR = (kTileRows * NSG + 31) / 32;
+    float sca[NSR];
+    {
+        const uint32_t g0 = c0 / p.group_size;
+#pragma unroll
+        for (int k = 0; k < NSR; ++k) {
+            const int v = 32 * k + lane;
+            const int r = v / NSG;
+            float sv = 0.f;
+            if (r < rows_here) sv = __half2float(p.scales[static_cast<size_t>(r0 + r) * p.ng + g0 + (v % NSG)]);
+            sca[k] = sv;
+        }
+    }
+    const uint32_t xcol = xsb + (c0 + lane) * (2u * NB);  // this lane's column of the tile, token block
+
+#pragma unroll 1
+    for (int r = 0; r < rows_here; ++r) {
+        float sreg = sca[0];
+        if constexpr (NSR > 1) {
+            const int k = (r * NSG) >> 5;
+#pragma unroll
+            for (int kk = 1; kk < NSR; ++kk) sreg = k == kk ? sca[kk] : sreg;
+        }
+        float racc[NB];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) racc[b] = 0.f;
+#pragma unroll 1
+        for (int sg = 0; sg < NSG; ++sg) {
+            __half2 gacc[NH];
+#pragma unroll
+            for (int h = 0; h < NH; ++h) gacc[h] = __float2half2_rn(0.f);
+#pragma unroll
+            for (int mm = 0; mm < GPL; ++mm) {
+                const int m = sg * GPL + mm;
+                uint32_t e;
+                if constexpr (CONSTANT) {
+                    e = cent;
+                } else {
+                    e = decode_step(x, a, tb);
+                }
+                // the sym field ORed into the mantissa of 64.0f is 64 + s/8
+                const float wf = __uint_as_float((e & 0x3C000u) | 0x42800000u) - 65.0f;  // (s - 8) / 8, exact
+                const __half2 w2 = __float2half2_rn(wf);
+                __half2 xh[NH];
+                lds_x<NB>(xcol + static_cast<uint32_t>(m) * (64u * NB), xh);
+#pragma unroll
+                for (int h = 0; h < NH; ++h) gacc[h] = __hfma2(w2, xh[h], gacc[h]);
+            }
+            const float gs = __shfl_sync(0xffffffffu, sreg, (r * NSG + sg) & 31);
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {
+                const float2 f = __half22float2(gacc[h]);
+                racc[2 * h] = fmaf(gs, f.x, racc[2 * h]);
+                racc[2 * h + 1] = fmaf(gs, f.y, racc[2 * h + 1]);
+            }
+        }
+        const float v = transpose_reduce<NB>(racc, lane);
+        if (reduce_owner<NB>(lane))
+            p.partials[(static_cast<size_t>(t) * kTileRows + r) * NB + reduce_index<NB>(lane)] = v;
+    }
+    // rows past a short slab contribute zeros
+    for (int r = rows_here; r < kTileRows; ++r)
+        if (lane < NB) p.partials[(static_cast<size_t>(t) * kTileRows + r) * NB + lane] = 0.f;
+    if constexpr (!CONSTANT) {
+        if (x != kL || (a - buf - lane) != len * 32u) atomicOr(p.status, ECQ_STATUS_CORRUPT);
+    } else {
+        if (len != 4u) atomicOr(p.status, ECQ_STATUS_CORRUPT);
+    }
+    complete_pending_batch<NB>(p, pend, lane);
+    // the owner lanes' partial stores are ordered before lane 0 counts the
+    // tile (the warp that completes the slab reads them after its own
+    // acquire-release increment)
+    __threadfence();
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atom_add_acq_rel(p.slab_count + slab, 1u);
+    pend.slab = slab;
+    pend.old = old;
+    pend.rows = rows_here;
+}
+
+// Shared memory: [decode table 64 KB][x][2 stage buffers per warp][read-ahead pad][mbarriers]
+template <int MPL, int GPL, int MODE, int NB = 1>
 __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
     constexpr bool GEMV = MODE == kModeGemv;
+    constexpr bool BATCH = MODE == kModeGemvBatch;
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int W = blockDim.x >> 5;
     const uint32_t sbase = smem_addr(smem);  // the decode table's shared-window address
-    const uint32_t bufs_off = kTableBytes + ((p.x_bytes + 127u) & ~127u);
+    const uint32_t bufs_off = kTableBytes + ((p.x_bytes + p.xs_bytes + 127u) & ~127u);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + bufs_off + 2 * W * p.buf_bytes + overrun_pad<MPL>());
     const uint32_t table_bar = smem_addr(bars + 2 * W);
     const bool constant = p.flags & ECQ_FLAG_CONSTANT;
@@ -410,6 +603,21 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
     // tile on their way
     pdl_wait();
     if (threadIdx.x == 0 && p.x_bytes) bulk_copy_g2s(sbase + kTableBytes, p.x, p.x_bytes, table_bar);
+    if constexpr (BATCH) {
+        // x of the NB tokens as fp16 x 8, [cols][NB], tokens past batch_here zero
+        __half* xs = reinterpret_cast<__half*>(smem + kTableBytes);
+        for (uint32_t c = threadIdx.x; c < p.cols; c += blockDim.x) {
+            __half v[NB];
+#pragma unroll
+            for (int b = 0; b < NB; ++b)
+                v[b] = b < static_cast<int>(p.batch_here)
+                           ? __hmul(p.x[static_cast<size_t>(b) * p.cols + c], __float2half(8.f))
+                           : __float2half(0.f);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) xs[static_cast<size_t>(c) * NB + b] = v[b];
+        }
+        __syncthreads();
+    }
     bool ok = mbar_wait(table_bar, 0);
     if (!ok && lane == 0) atomicOr(p.status, ECQ_STATUS_TIMEOUT);
 
@@ -433,12 +641,20 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
         if (stage) phase1 ^= 1; else phase0 ^= 1;
         uint32_t buf = sbase + my_buf0 + stage * p.buf_bytes;
         asm volatile("" : "+r"(buf)::"memory");  // keep this tile's byte loads after its wait
-        if (constant)
-            process_tile<MPL, GPL, MODE, true>(p, t, buf, sbase, lane, pend);
-        else
-            process_tile<MPL, GPL, MODE, false>(p, t, buf, sbase, lane, pend);
+        if constexpr (BATCH) {
+            if (constant)
+                process_tile_batch<MPL, GPL, NB, true>(p, t, buf, sbase, sbase + kTableBytes, lane, pend);
+            else
+                process_tile_batch<MPL, GPL, NB, false>(p, t, buf, sbase, sbase + kTableBytes, lane, pend);
+        } else {
+            if (constant)
+                process_tile<MPL, GPL, MODE, true>(p, t, buf, sbase, lane, pend);
+            else
+                process_tile<MPL, GPL, MODE, false>(p, t, buf, sbase, lane, pend);
+        }
     }
     if constexpr (GEMV) complete_pending(p, pend, lane);
+    if constexpr (BATCH) complete_pending_batch<NB>(p, pend, lane);
     // never leave a bulk copy in flight when exiting after a timeout
     if (!ok && t_begin < t_end) {
         mbar_wait(my_bar0, phase0);
@@ -451,10 +667,10 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
 // ---------------------------------------------------------------------------
 using KernelFn = void (*)(MatrixParams);
 
-template <int MODE>
+template <int MODE, int NB = 1>
 KernelFn pick_kernel(int mpl, int gpl) {
 #define ECQ_CASE(M_, G_) \
-    if (mpl == M_ && gpl == G_) return matrix_kernel<M_, G_, MODE>;
+    if (mpl == M_ && gpl == G_) return matrix_kernel<M_, G_, MODE, NB>;
     ECQ_CASE(4, 1) ECQ_CASE(4, 2) ECQ_CASE(4, 4)
     ECQ_CASE(8, 1) ECQ_CASE(8, 2) ECQ_CASE(8, 4) ECQ_CASE(8, 8)
     ECQ_CASE(16, 1) ECQ_CASE(16, 2) ECQ_CASE(16, 4) ECQ_CASE(16, 8) ECQ_CASE(16, 16)
@@ -462,22 +678,40 @@ KernelFn pick_kernel(int mpl, int gpl) {
     return nullptr;
 }
 
+KernelFn pick_mode(int mode, int nb, int mpl, int gpl) {
+    switch (mode) {
+        case kModeSymbols: return pick_kernel<kModeSymbols>(mpl, gpl);
+        case kModeGemv: return pick_kernel<kModeGemv>(mpl, gpl);
+        case kModeWeights: return pick_kernel<kModeWeights>(mpl, gpl);
+        case kModePacked4: return pick_kernel<kModePacked4>(mpl, gpl);
+        case kModeGemvBatch:
+            if (nb == 2) return pick_kernel<kModeGemvBatch, 2>(mpl, gpl);
+            if (nb == 4) return pick_kernel<kModeGemvBatch, 4>(mpl, gpl);
+            if (nb == 8) return pick_kernel<kModeGemvBatch, 8>(mpl, gpl);
+            return nullptr;
+    }
+    return nullptr;
+}
+
 struct LaunchShape {
     int mpl, gpl, warps, ctas;
     uint32_t buf_bytes;
     size_t smem;
-    uint32_t x_bytes;
+    uint32_t x_bytes;   // x bulk-copied into shared memory (GEMV)
+    uint32_t xs_bytes;  // x of nb tokens staged as fp16 [cols][nb] (batched GEMV)
 };
 
-// groups: the kernel applies group scales (GEMV or fp16 weights); stage_x: GEMV
-int32_t shape_for(const ecq_matrix_view* m, bool groups, bool stage_x, LaunchShape* ls, bool packed = false) {
-    const bool gemv = groups;
+constexpr int kMinBatchWarps = 16;  // a batched launch keeps at least this many warps per CTA
+
+// mode: what the kernel does (kMode*); nb: tokens per launch (batched GEMV)
+int32_t shape_for(const ecq_matrix_view* m, int mode, int nb, LaunchShape* ls) {
     if (!m) return ECQ_ERR_ARG;
+    const bool groups = mode == kModeGemv || mode == kModeWeights || mode == kModeGemvBatch;
     if (m->tile_rows != kTileRows) return ECQ_ERR_UNSUPPORTED;
     if (m->tile_cols % 32 || m->tile_cols == 0 || m->cols % m->tile_cols) return ECQ_ERR_SHAPE;
     const int mpl = static_cast<int>(m->tile_cols / 32);
     int gpl = mpl;
-    if (gemv) {
+    if (groups) {
         const uint32_t g = m->group_size;
         if (g == 0 || g % 32) return ECQ_ERR_UNSUPPORTED;
         if (g < m->tile_cols) {
@@ -487,21 +721,25 @@ int32_t shape_for(const ecq_matrix_view* m, bool groups, bool stage_x, LaunchSha
             return ECQ_ERR_UNSUPPORTED;
         }
     }
-    if (!(stage_x ? pick_kernel<kModeGemv>(mpl, gpl)
-                  : (groups ? pick_kernel<kModeWeights>(mpl, gpl)
-                            : (packed ? pick_kernel<kModePacked4>(mpl, gpl) : pick_kernel<kModeSymbols>(mpl, gpl)))))
-        return ECQ_ERR_UNSUPPORTED;
+    if (!pick_mode(mode, nb, mpl, gpl)) return ECQ_ERR_UNSUPPORTED;
     const uint32_t slabs = (m->rows + kTileRows - 1) / kTileRows;
     if (m->n_tiles != slabs * (m->cols / m->tile_cols)) return ECQ_ERR_SHAPE;
     uint32_t buf = (m->max_tile_bytes + 127u) & ~127u;
     if (buf < 128) buf = 128;
     const int bar_bytes = 8 * (2 * 32 + 1);
     const int pad = static_cast<int>((32u * (5u + 3u * kTileRows * static_cast<uint32_t>(mpl)) + 127u) & ~127u);
-    // stage x in shared memory when it leaves room for at least 16 warps
-    uint32_t xb = stage_x ? m->cols * 2u : 0u;
-    if (xb > static_cast<uint32_t>(kMaxSmem - kTableBytes - pad - bar_bytes) - 16u * 2u * buf) xb = 0;
-    const int xpad = static_cast<int>((xb + 127u) & ~127u);
-    int warps = static_cast<int>((kMaxSmem - kTableBytes - xpad - pad - bar_bytes) / (2 * static_cast<int64_t>(buf)));
+    const int64_t room = kMaxSmem - kTableBytes - pad - bar_bytes;
+    uint32_t xb = 0, xsb = 0;
+    if (mode == kModeGemv) {
+        // stage x in shared memory when it leaves room for at least 16 warps
+        xb = m->cols * 2u;
+        if (xb > room - 16 * 2 * static_cast<int64_t>(buf)) xb = 0;
+    } else if (mode == kModeGemvBatch) {
+        xsb = m->cols * 2u * static_cast<uint32_t>(nb);
+        if (xsb > room - kMinBatchWarps * 2 * static_cast<int64_t>(buf)) return ECQ_ERR_UNSUPPORTED;
+    }
+    const int xpad = static_cast<int>((xb + xsb + 127u) & ~127u);
+    int warps = static_cast<int>((room - xpad) / (2 * static_cast<int64_t>(buf)));
     if (warps > 32) warps = 32;
     if (warps < 1) return ECQ_ERR_UNSUPPORTED;
     ls->mpl = mpl;
@@ -511,25 +749,61 @@ int32_t shape_for(const ecq_matrix_view* m, bool groups, bool stage_x, LaunchSha
     ls->buf_bytes = buf;
     ls->smem = static_cast<size_t>(2 * warps) * buf + kTableBytes + xpad + pad + 8 * (2 * warps + 1);
     ls->x_bytes = xb;
+    ls->xs_bytes = xsb;
     return ECQ_OK;
 }
 
-int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, const __half* scales, __half* y,
-                      uint8_t* sym_out, void* workspace, uint32_t* status, cudaStream_t stream,
-                      __half* w_out = nullptr, const ecq_tp_comm* comm = nullptr, bool packed = false) {
+// tokens one batched-GEMV launch takes for this batch: the largest of 8, 4, 2
+// (not above the batch rounded up to a power of two) whose staged x leaves
+// room for kMinBatchWarps warps; 1 when batch is 1 or none fits (then each
+// token runs the single-token GEMV)
+int gemv_tokens(const ecq_matrix_view* m, uint32_t batch) {
+    if (batch <= 1) return 1;
+    int nb = batch >= 8 ? 8 : (batch > 2 ? (batch > 4 ? 8 : 4) : 2);
+    for (; nb >= 2; nb >>= 1) {
+        LaunchShape ls;
+        if (shape_for(m, kModeGemvBatch, nb, &ls) == ECQ_OK) return nb;
+    }
+    return 1;
+}
+
+// GEMV workspace: [slab counters, n_slabs u32 (rounded up to 16 bytes)]
+// [partials, n_tiles x 8 rows x nb fp32]. The counters come first so that
+// their place does not depend on the tile count or the tokens per launch.
+size_t ws_counter_bytes(const ecq_matrix_view* m) {
+    const size_t slabs = (m->rows + kTileRows - 1) / kTileRows;
+    return (slabs * 4 + 15) & ~static_cast<size_t>(15);
+}
+int64_t ws_bytes(const ecq_matrix_view* m, int nb) {
+    return static_cast<int64_t>(ws_counter_bytes(m)) + static_cast<int64_t>(m->n_tiles) * kTileRows * 4 * nb;
+}
+
+struct LaunchArgs {
+    const __half* x = nullptr;
+    const __half* scales = nullptr;
+    __half* y = nullptr;
+    uint8_t* sym_out = nullptr;
+    __half* w_out = nullptr;
+    void* workspace = nullptr;
+    const ecq_tp_comm* comm = nullptr;
+    uint32_t batch_here = 1;
+};
+
+int32_t launch_matrix(const ecq_matrix_view* m, int mode, int nb, const LaunchArgs& la, uint32_t* status,
+                      cudaStream_t stream) {
     LaunchShape ls;
-    int32_t rc = shape_for(m, gemv || w_out != nullptr, gemv, &ls, packed);
+    int32_t rc = shape_for(m, mode, nb, &ls);
     if (rc != ECQ_OK) return rc;
     MatrixParams p{};
     p.data = m->data;
     p.tile_offset = m->tile_offset;
     p.stream_len = m->stream_len;
     p.dec_table = m->dec_table;
-    p.x = x;
-    p.scales = scales;
-    p.y = y;
-    p.sym_out = sym_out;
-    p.w_out = w_out;
+    p.x = la.x;
+    p.scales = la.scales;
+    p.y = la.y;
+    p.sym_out = la.sym_out;
+    p.w_out = la.w_out;
     p.status = status;
     p.rows = m->rows;
     p.cols = m->cols;
@@ -540,23 +814,22 @@ int32_t launch_matrix(const ecq_matrix_view* m, bool gemv, const __half* x, cons
     p.buf_bytes = ls.buf_bytes;
     p.flags = m->flags;
     // x staged by bulk copy needs a 16-byte aligned address
-    p.x_bytes = (gemv && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) ? ls.x_bytes : 0u;
-    if (gemv) {
-        p.partials = static_cast<float*>(workspace);
-        p.slab_count = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) +
-                                                   static_cast<size_t>(m->n_tiles) * kTileRows * sizeof(float));
+    p.x_bytes = (mode == kModeGemv && (reinterpret_cast<uintptr_t>(la.x) & 15u) == 0) ? ls.x_bytes : 0u;
+    p.xs_bytes = ls.xs_bytes;
+    p.nb = static_cast<uint32_t>(nb);
+    p.batch_here = la.batch_here;
+    if (mode == kModeGemv || mode == kModeGemvBatch) {
+        p.slab_count = static_cast<uint32_t*>(la.workspace);
+        p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(la.workspace) + ws_counter_bytes(m));
     }
-    if (comm) {
-        p.tp_world = comm->world;
-        p.tp_rank = comm->rank;
-        p.tp_nmax = comm->n_max;
-        p.tp_epoch = static_cast<uint32_t*>(comm->local);
-        for (uint32_t q = 0; q < comm->world; ++q) p.tp_peer[q] = static_cast<uint8_t*>(comm->peers[q]);
+    if (la.comm) {
+        p.tp_world = la.comm->world;
+        p.tp_rank = la.comm->rank;
+        p.tp_nmax = la.comm->n_max;
+        p.tp_epoch = static_cast<uint32_t*>(la.comm->local);
+        for (uint32_t q = 0; q < la.comm->world; ++q) p.tp_peer[q] = static_cast<uint8_t*>(la.comm->peers[q]);
     }
-    KernelFn fn = gemv ? pick_kernel<kModeGemv>(ls.mpl, ls.gpl)
-                       : (w_out ? pick_kernel<kModeWeights>(ls.mpl, ls.gpl)
-                                : (packed ? pick_kernel<kModePacked4>(ls.mpl, ls.gpl)
-                                          : pick_kernel<kModeSymbols>(ls.mpl, ls.gpl)));
+    KernelFn fn = pick_mode(mode, nb, ls.mpl, ls.gpl);
     if (!ensure_smem_limit(reinterpret_cast<const void*>(fn), kMaxSmem)) return ECQ_ERR_CUDA;
     if (launch_pdl(fn, dim3(ls.ctas), dim3(ls.warps * 32), ls.smem, stream, p) != cudaSuccess) {
         cudaGetLastError();
@@ -590,14 +863,16 @@ int32_t ecq_decode_interleaved(const uint8_t* d_data, const uint32_t* d_lengths,
 
 int32_t ecq_matrix_decode(const ecq_matrix_view* m, uint8_t* d_out, uint32_t* d_status, void* stream) {
     if (!view_ok(m) || !d_out || !d_status) return ECQ_ERR_ARG;
-    return launch_matrix(m, false, nullptr, nullptr, nullptr, d_out, nullptr, d_status,
-                         static_cast<cudaStream_t>(stream));
+    LaunchArgs la;
+    la.sym_out = d_out;
+    return launch_matrix(m, kModeSymbols, 1, la, d_status, static_cast<cudaStream_t>(stream));
 }
 
 int32_t ecq_matrix_decode_packed4(const ecq_matrix_view* m, uint8_t* d_out, uint32_t* d_status, void* stream) {
     if (!view_ok(m) || !d_out || !d_status) return ECQ_ERR_ARG;
-    return launch_matrix(m, false, nullptr, nullptr, nullptr, d_out, nullptr, d_status,
-                         static_cast<cudaStream_t>(stream), nullptr, nullptr, true);
+    LaunchArgs la;
+    la.sym_out = d_out;
+    return launch_matrix(m, kModePacked4, 1, la, d_status, static_cast<cudaStream_t>(stream));
 }
 
 int32_t ecq_matrix_dequantize(const ecq_matrix_view* m, const void* scales_f16, void* w_out_f16, uint32_t* d_status,
@@ -606,28 +881,40 @@ int32_t ecq_matrix_dequantize(const ecq_matrix_view* m, const void* scales_f16, 
     if (m->group_size == 0 || m->group_size % 32 || (m->group_size < m->tile_cols && m->tile_cols % m->group_size) ||
         (m->group_size >= m->tile_cols && m->group_size % m->tile_cols))
         return ECQ_ERR_UNSUPPORTED;
-    return launch_matrix(m, false, nullptr, static_cast<const __half*>(scales_f16), nullptr, nullptr, nullptr,
-                         d_status, static_cast<cudaStream_t>(stream), static_cast<__half*>(w_out_f16));
+    LaunchArgs la;
+    la.scales = static_cast<const __half*>(scales_f16);
+    la.w_out = static_cast<__half*>(w_out_f16);
+    return launch_matrix(m, kModeWeights, 1, la, d_status, static_cast<cudaStream_t>(stream));
 }
 
 int64_t ecq_gemv_workspace_bytes(const ecq_matrix_view* m, uint32_t batch) {
-    (void)batch;
     if (!m || !m->rows || !m->n_tiles) return ECQ_ERR_ARG;
-    const int64_t slabs = (m->rows + kTileRows - 1) / kTileRows;
-    return static_cast<int64_t>(m->n_tiles) * kTileRows * 4 + slabs * 4;
+    return ws_bytes(m, gemv_tokens(m, batch));
 }
 
 int32_t ecq_gemv(const ecq_matrix_view* m, const void* x_f16, const void* scales_f16, void* y_f16, uint32_t batch,
                  void* workspace, int64_t workspace_bytes, uint32_t* d_status, void* stream) {
     if (!view_ok(m) || !x_f16 || !scales_f16 || !y_f16 || !d_status || batch == 0) return ECQ_ERR_ARG;
-    if (!workspace || workspace_bytes < ecq_gemv_workspace_bytes(m, batch)) return ECQ_ERR_WORKSPACE;
+    if (!workspace || workspace_bytes < ws_bytes(m, 1)) return ECQ_ERR_WORKSPACE;
     const __half* x = static_cast<const __half*>(x_f16);
     __half* y = static_cast<__half*>(y_f16);
-    for (uint32_t b = 0; b < batch; ++b) {
-        int32_t rc = launch_matrix(m, true, x + static_cast<size_t>(b) * m->cols, static_cast<const __half*>(scales_f16),
-                                   y + static_cast<size_t>(b) * m->rows, nullptr, workspace, d_status,
-                                   static_cast<cudaStream_t>(stream));
+    LaunchArgs la;
+    la.scales = static_cast<const __half*>(scales_f16);
+    la.workspace = workspace;
+    // token batches: up to nb tokens per launch share one decode of every
+    // tile; a workspace sized for fewer tokens runs the single-token GEMV
+    int nb = gemv_tokens(m, batch);
+    while (nb > 1 && workspace_bytes < ws_bytes(m, nb)) nb >>= 1;
+    for (uint32_t b = 0; b < batch;) {
+        const uint32_t here = nb > 1 ? std::min<uint32_t>(static_cast<uint32_t>(nb), batch - b) : 1u;
+        la.x = x + static_cast<size_t>(b) * m->cols;
+        la.y = y + static_cast<size_t>(b) * m->rows;
+        la.batch_here = here;
+        // a last chunk of one token takes the exact single-token kernel
+        const int mode = here > 1 ? kModeGemvBatch : kModeGemv;
+        int32_t rc = launch_matrix(m, mode, here > 1 ? nb : 1, la, d_status, static_cast<cudaStream_t>(stream));
         if (rc != ECQ_OK) return rc;
+        b += here;
     }
     return ECQ_OK;
 }
@@ -640,9 +927,13 @@ int32_t ecq_gemv_tp(const ecq_matrix_view* m, const void* x_f16, const void* sca
         return ECQ_ERR_ARG;
     for (uint32_t q = 0; q < comm->world; ++q)
         if (!comm->peers[q]) return ECQ_ERR_ARG;
-    if (!workspace || workspace_bytes < ecq_gemv_workspace_bytes(m, 1)) return ECQ_ERR_WORKSPACE;
-    return launch_matrix(m, true, static_cast<const __half*>(x_f16), static_cast<const __half*>(scales_f16), nullptr,
-                         nullptr, workspace, d_status, static_cast<cudaStream_t>(stream), nullptr, comm);
+    if (!workspace || workspace_bytes < ws_bytes(m, 1)) return ECQ_ERR_WORKSPACE;
+    LaunchArgs la;
+    la.x = static_cast<const __half*>(x_f16);
+    la.scales = static_cast<const __half*>(scales_f16);
+    la.workspace = workspace;
+    la.comm = comm;
+    return launch_matrix(m, kModeGemv, 1, la, d_status, static_cast<cudaStream_t>(stream));
 }
 
 int32_t ecq_device_info(int32_t* sm_count, int32_t* gemv_ctas, int32_t* gemv_warps_per_cta,
@@ -650,7 +941,7 @@ int32_t ecq_device_info(int32_t* sm_count, int32_t* gemv_ctas, int32_t* gemv_war
     if (sm_count) *sm_count = sm_count_cached();
     if (m) {
         LaunchShape ls;
-        int32_t rc = shape_for(m, true, true, &ls);
+        int32_t rc = shape_for(m, kModeGemv, 1, &ls);
         if (rc != ECQ_OK) return rc;
         if (gemv_ctas) *gemv_ctas = ls.ctas;
         if (gemv_warps_per_cta) *gemv_warps_per_cta = ls.warps;
@@ -753,15 +1044,12 @@ extern "C" int32_t ecq_gemv_noalloc(const ecq_matrix_view* m, const void* x_f16,
     void* scratch = nullptr;
     const int32_t rc = noalloc_scratch(&scratch);
     if (rc != ECQ_OK) return rc;
-    // The per-slab completion counters follow the per-tile partial sums, so
-    // where they sit depends on this matrix's tile count: a call on a smaller
-    // matrix after a larger one finds its counters inside the larger one's
-    // partial sums, and a call that failed may leave counters set. Clear them
-    // on every call (the partial sums need no clearing: each is written
-    // before it is read).
-    const int64_t counters = static_cast<int64_t>(m->n_tiles) * kTileRows * static_cast<int64_t>(sizeof(float));
-    if (cudaMemsetAsync(static_cast<uint8_t*>(scratch) + counters, 0, static_cast<size_t>(need - counters),
-                        static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    // The per-slab completion counters sit at the start of the workspace. A
+    // finished call leaves them zero, but the array keeps whatever the last
+    // call left, including one that failed: clear them on every call (the
+    // partial sums after them need no clearing: each is written before it is
+    // read).
+    if (cudaMemsetAsync(scratch, 0, ws_counter_bytes(m), static_cast<cudaStream_t>(stream)) != cudaSuccess)
         return ECQ_ERR_CUDA;
     return ecq_gemv(m, x_f16, scales_f16, y_f16, batch, scratch, need, d_status, stream);
 }

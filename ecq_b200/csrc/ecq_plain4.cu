@@ -207,10 +207,15 @@ struct Plain4Shape {
     int warps, rows_per_warp;
 };
 
-// Launch shape: 4-warp CTAs with 2 rows per warp and 4 chunks of each row in
-// flight per lane (one token); token batches take 1 row per warp.
-Plain4Shape pick_plain4(int B) {
-    if (B == 1) return {plain4_gemv_kernel<4, 2, 4, 1>, 4, 2};
+// Launch shape (one token), measured on the Llama-7B sweep shapes: 8-warp
+// CTAs with one row per warp for up to 8191 rows, 4-warp CTAs with two rows
+// per warp above; 4 chunks of each row in flight per lane. Token batches
+// take one row per warp.
+Plain4Shape pick_plain4(int B, uint32_t rows) {
+    if (B == 1) {
+        if (rows >= 8192) return {plain4_gemv_kernel<4, 2, 4, 1>, 4, 2};
+        return {plain4_gemv_kernel<8, 1, 4, 1>, 8, 1};
+    }
     if (B == 2) return {plain4_gemv_kernel<4, 1, 4, 2>, 4, 1};
     if (B == 3) return {plain4_gemv_kernel<4, 1, 2, 3>, 4, 1};
     return {plain4_gemv_kernel<4, 1, 2, 4>, 4, 1};
@@ -238,7 +243,7 @@ extern "C" int32_t ecq_plain4_gemv(const void* q_packed, const void* scales_f16,
     for (uint32_t b0 = 0; b0 < batch;) {
         const int B = static_cast<int>(min(min(4u, fit), batch - b0));
         const size_t smem = static_cast<size_t>(B) * cols * 2u;
-        const Plain4Shape ps = pick_plain4(B);
+        const Plain4Shape ps = pick_plain4(B, rows);
         if (!ensure_smem_limit(reinterpret_cast<const void*>(ps.fn), kMaxSmem)) return ECQ_ERR_CUDA;
         const uint32_t per_cta = static_cast<uint32_t>(ps.warps * ps.rows_per_warp);
         const dim3 grid((rows + per_cta - 1) / per_cta);

@@ -30,6 +30,11 @@ def _require_cuda(t: torch.Tensor, name: str) -> None:
         raise ValueError(f"{name} must be contiguous")
 
 
+# Token batches up to this size run the fused GEMV (each tile decoded once per
+# up to 8 tokens); larger ones a tensor-core path.
+GEMV_MAX_BATCH = 8
+
+
 @dataclass
 class DeviceMatrix:
     rows: int
@@ -157,11 +162,13 @@ class DeviceMatrix:
                                self.mm_workspace.numel(), ptr(self.status), _stream_ptr(stream)), "matmul")
         return out
 
-    def matmul(self, x: torch.Tensor, scales: torch.Tensor, fused_max_batch: int = 1) -> torch.Tensor:
-        """y = x @ W^T for x [..., cols] fp16. Up to `fused_max_batch` rows run
-        the fused GEMV per row. Larger batches run the tcgen05 kernel
-        (matmul_tc) when the tile layout has one (tile widths 128 and 256);
-        8x512 tiles decode W once to fp16 (dequantize) for a tensor-core GEMM."""
+    def matmul(self, x: torch.Tensor, scales: torch.Tensor, fused_max_batch: int = GEMV_MAX_BATCH) -> torch.Tensor:
+        """y = x @ W^T for x [..., cols] fp16: the one dispatch every batched
+        entry point uses. Up to `fused_max_batch` token rows run the fused
+        GEMV, which decodes each tile once for up to 8 tokens. Larger batches
+        run the tcgen05 kernel (matmul_tc) when the tile layout has one (tile
+        widths 128 and 256); otherwise W is decoded once to fp16
+        (dequantize) for a tensor-core GEMM."""
         lead = x.shape[:-1]
         x2 = x.reshape(-1, self.cols)
         if x2.shape[0] <= fused_max_batch:
@@ -172,6 +179,14 @@ class DeviceMatrix:
             w = self.dequantize(scales)
             y = torch.mm(x2, w.t(), out_dtype=torch.float32).to(torch.float16)
         return y.reshape(*lead, self.rows)
+
+    def ensure_workspace(self, batch: int) -> None:
+        """Grow the GEMV workspace (zero-filled) to what a `batch`-token call
+        needs. Call it outside stream capture before capturing such calls."""
+        need = int(lib().ecq_gemv_workspace_bytes(self.view(), int(batch)))
+        check(need, "workspace size")
+        if self.workspace.numel() < need:
+            self.workspace = torch.zeros(need, dtype=torch.uint8, device=self.device)
 
     def gemv(self, x: torch.Tensor, scales: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
         """y[b] = W_deq x[b] (fp16 in/out, fp32 accumulation); x [B, cols] or [cols]."""
@@ -188,6 +203,8 @@ class DeviceMatrix:
         if out is None:
             out = torch.empty(B, self.rows, dtype=torch.float16, device=self.device)
         _require_cuda(out, "out")
+        if B > 1 and not torch.cuda.is_current_stream_capturing():
+            self.ensure_workspace(B)
         v = self.view()
         check(lib().ecq_gemv(v, ptr(x2), ptr(scales), ptr(out), B, ptr(self.workspace), self.workspace.numel(),
                              ptr(self.status), _stream_ptr(stream)), "gemv")

@@ -18,7 +18,7 @@ import torch
 from . import _lib
 from ._lib import MatrixView, check, lib
 from .codec import RANSTable, encode_matrix
-from .device import DeviceMatrix, Packed4Matrix
+from .device import GEMV_MAX_BATCH, DeviceMatrix, Packed4Matrix
 from .synthetic import quantize_symmetric_groups
 
 
@@ -55,7 +55,11 @@ def _(x, data, tile_offset, stream_len, dec_table, scales, workspace, status, ro
 
 
 def rans_gemv(x: torch.Tensor, m: DeviceMatrix, scales: torch.Tensor) -> torch.Tensor:
-    """The custom op on a DeviceMatrix; x [B, cols] or [cols] fp16."""
+    """The custom op on a DeviceMatrix; x [B, cols] or [cols] fp16. Token
+    batches share one decode of each tile (up to 8 tokens per launch)."""
+    B = x.numel() // m.cols
+    if B > 1 and not torch.cuda.is_current_stream_capturing():
+        m.ensure_workspace(B)
     y = torch.ops.ecq.rans_gemv(x, m.data, m.tile_offset, m.stream_len, m.dec_table, scales, m.workspace,
                                 m.status, m.rows, m.cols, m.tile_rows, m.tile_cols, m.group_size, m.flags,
                                 m.max_tile_bytes)
@@ -89,11 +93,16 @@ def _(x, data, tile_offset, stream_len, dec_table, scales, workspace, status, ro
 
 
 def rans_matmul(x: torch.Tensor, m: DeviceMatrix, scales: torch.Tensor) -> torch.Tensor:
-    """x [B, cols] fp16 -> y [B, rows]: the tcgen05 kernel when the matrix's
-    tile layout has one, else the fused GEMV per token row."""
+    """x [B, cols] fp16 -> y [B, rows], routed as DeviceMatrix.matmul routes:
+    up to GEMV_MAX_BATCH tokens the fused GEMV (each tile decoded once for up
+    to 8 tokens), more the tcgen05 kernel when the tile layout has one, else
+    W decoded once to fp16 for a tensor-core GEMM."""
     x2 = x.reshape(-1, m.cols)
-    if x2.shape[0] < 2 or not m.tensor_core_ok():
+    if x2.shape[0] <= GEMV_MAX_BATCH:
         return rans_gemv(x2.contiguous(), m, scales)
+    if not m.tensor_core_ok():
+        w = m.dequantize(scales)
+        return torch.mm(x2.contiguous(), w.t(), out_dtype=torch.float32).to(torch.float16)
     need = int(lib().ecq_matmul_workspace_bytes(m.view(), x2.shape[0]))
     check(need, "matmul workspace size")
     if m.mm_workspace is None or m.mm_workspace.numel() < need:

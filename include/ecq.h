@@ -171,10 +171,15 @@ int32_t ecq_matrix_dequantize(const ecq_matrix_view *m, const void *scales_f16, 
 
 /* ---------------- device: fused decode + dequant + GEMV ---------------- */
 
-/* Bytes of device workspace ecq_gemv needs for this matrix and batch. The
- * workspace must be zero-filled once before first use; ecq_gemv leaves it
- * zeroed again on completion, so it can be reused across calls on one
- * stream (calls that overlap on the GPU must use distinct workspaces). */
+/* Bytes of device workspace ecq_gemv needs for this matrix and batch:
+ * ceil(ceil(rows/8) * 4 / 16) * 16 bytes of slab counters, then
+ * n_tiles * 32 * nb bytes of partial sums, nb being the tokens one launch
+ * takes (1 for batch 1; 8, 4 or 2 for token batches, as many as x of that
+ * many tokens fits in shared memory). The workspace must be zero-filled once
+ * before first use; ecq_gemv leaves the counters zero again on completion,
+ * so it can be reused across calls on one stream (calls that overlap on the
+ * GPU must use distinct workspaces). A workspace sized for batch 1 also
+ * serves larger batches, token by token. */
 int64_t ecq_gemv_workspace_bytes(const ecq_matrix_view *m, uint32_t batch);
 
 /* y[b, r] = sum_c (sym[r,c] - 8) * scales[r, c/g] * x[b, c], fp32
@@ -185,7 +190,10 @@ int64_t ecq_gemv_workspace_bytes(const ecq_matrix_view *m, uint32_t batch);
  * the fused kernels fused_parallel_gemv / fused_parallel_gemv_cached /
  * tiled_parallel_gemm (src/metal_interleaved.py:130-484) and the MLX-side
  * entropy_coded_matmul (docs/mlx_integration_plan.md:222-237). No decoded
- * weight is written to memory. */
+ * weight is written to memory. For batch > 1 each launch decodes every tile
+ * once for up to 8 tokens (x staged in shared memory as fp16 x 8, so
+ * |x| < 8188; products summed in fp16 over the 1-16 symbols a lane holds of
+ * one scale group, then in fp32); batch 1 is all fp32. */
 int32_t ecq_gemv(const ecq_matrix_view *m, const void *x_f16, const void *scales_f16, void *y_f16,
                  uint32_t batch, void *workspace, int64_t workspace_bytes, uint32_t *d_status, void *stream);
 
@@ -201,16 +209,17 @@ int32_t ecq_gemv(const ecq_matrix_view *m, const void *x_f16, const void *scales
  *
  * The workspace comes from a fixed array inside the library
  * (ECQ_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the library until
- * exit). A matrix fits when ecq_gemv_workspace_bytes(m, 1) =
- * n_tiles * 32 + ceil(rows / 8) * 4 <= ECQ_NOALLOC_SCRATCH_BYTES (between
- * ~116.5K tiles, one K-tile per row slab, and ~130K, 16 per slab; e.g.
- * 28672 x 8192 in 8x512 tiles); larger ones are rejected with
- * ECQ_ERR_WORKSPACE before anything is launched. Nothing is allocated, by
+ * exit). A call fits when ecq_gemv_workspace_bytes(m, batch) <=
+ * ECQ_NOALLOC_SCRATCH_BYTES: for one token n_tiles * 32 plus the slab
+ * counters (~116.5K tiles with one K-tile per row slab to ~130K with 16,
+ * e.g. 28672 x 8192 in 8x512 tiles), and nb times the partial sums for token
+ * batches; larger calls are rejected with ECQ_ERR_WORKSPACE before anything
+ * is launched. Nothing is allocated, by
  * the library or anyone else. The first call on each device looks up the
  * array's device address (cudaGetSymbolAddress, with that device current);
  * make that first call before any stream capture. The address is looked up
  * again when the current CUDA context changes (e.g. after cudaDeviceReset),
- * and every call clears the matrix's slab counters in the array with a
+ * and every call clears the slab counters at the start of the array with a
  * cudaMemsetAsync on the caller's stream. Every call shares the array: calls whose
  * kernels may overlap on the GPU (other streams, other host threads) race
  * and must be serialised by the caller. Arguments and results are those of

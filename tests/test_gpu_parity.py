@@ -145,15 +145,63 @@ def test_corrupt_packed_tile_sets_status():
     assert m.read_status() & 1
 
 
-def test_batched_gemv():
-    sym = syn.laplace_symbols(96, 1024, b=0.5, seed=4)
-    sc = syn.group_scales(96, 1024, 128)
-    x = syn.activations(4, 1024)
+@pytest.mark.parametrize("M,K,tc,g,B", [
+    (96, 1024, 512, 128, 4),      # one launch of 4 tokens
+    (520, 2048, 512, 128, 8),     # 8 tokens, a short last row slab
+    (264, 768, 256, 64, 3),       # 3 tokens in a 4-token launch (one zero token)
+    (200, 1024, 128, 32, 5),      # 8-token launch, 8x128 tiles, group 32
+    (512, 4096, 512, 256, 9),     # 8 + 1 (the last token on the single-token kernel)
+    (1024, 11008, 256, 128, 16),  # x of 8 tokens does not fit next to 11008 columns: 4 launches of 4
+    (64, 512, 512, 512, 2),       # group = tile width
+])
+def test_batched_gemv_decodes_each_tile_once(M, K, tc, g, B):
+    """Token batches share one decode of each tile (up to 8 tokens per
+    launch); every token's y against the float64 oracle, and bit-identical
+    replays."""
+    sym = syn.laplace_symbols(M, K, b=0.5, seed=M + B)
+    sc = syn.group_scales(M, K, g, seed=K)
+    x = syn.activations(B, K, seed=B)
+    m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, tile_cols=tc, group_size=g), group_size=g)
+    xs, ss = torch.from_numpy(x).cuda(), torch.from_numpy(sc).cuda()
+    y = m.gemv(xs, ss).clone()
+    y2 = m.gemv(xs, ss)
+    m.check()
+    assert torch.equal(y, y2)
+    y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), g, x.astype(np.float32))
+    assert y.shape == (B, M) and _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL
+
+
+def test_batched_gemv_student_t_constant_and_small_workspace():
+    # Student-t weights (wide symbol spread), a constant matrix, and a caller
+    # workspace sized for one token (the batch then runs token by token)
+    w = syn.student_t_weights(300, 2048, seed=3).astype(np.float32)
+    sym, sc = syn.quantize_symmetric_groups(w, 128)
+    x = syn.activations(6, 2048, seed=4)
     m = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, group_size=128), group_size=128)
     y = m.gemv(torch.from_numpy(x).cuda(), torch.from_numpy(sc).cuda())
     m.check()
     y_ref = oracle.dequant_gemv(sym, sc.astype(np.float32), 128, x.astype(np.float32))
     assert _rel_err(y.float().cpu().numpy(), y_ref) <= RTOL
+    from ecq_b200 import _lib
+
+    m1 = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(sym, group_size=128), group_size=128)
+    y1 = torch.empty(6, 300, dtype=torch.float16, device="cuda")
+    ws1 = torch.zeros(int(_lib.lib().ecq_gemv_workspace_bytes(m1.view(), 1)), dtype=torch.uint8, device="cuda")
+    xs = torch.from_numpy(x).cuda()
+    ss = torch.from_numpy(sc).cuda()
+    rc = _lib.lib().ecq_gemv(m1.view(), _lib.ptr(xs), _lib.ptr(ss), _lib.ptr(y1), 6, _lib.ptr(ws1), ws1.numel(),
+                             _lib.ptr(m1.status), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    m1.check()
+    assert _rel_err(y1.float().cpu().numpy(), y_ref) <= RTOL
+    const = np.full((40, 512), 5, dtype=np.uint8)
+    mc = ecq.DeviceMatrix.from_encoded(ecq.encode_matrix(const, group_size=128), group_size=128)
+    sc_c = syn.group_scales(40, 512, 128, seed=6)
+    xc = syn.activations(4, 512, seed=7)
+    yc = mc.gemv(torch.from_numpy(xc).cuda(), torch.from_numpy(sc_c).cuda())
+    mc.check()
+    assert _rel_err(yc.float().cpu().numpy(), oracle.dequant_gemv(const, sc_c.astype(np.float32), 128,
+                                                                   xc.astype(np.float32))) <= RTOL
 
 
 @pytest.mark.parametrize("M,K", [(4096, 4096), (11008, 4096), (4096, 11008)])
