@@ -30,9 +30,11 @@ def _require_cuda(t: torch.Tensor, name: str) -> None:
         raise ValueError(f"{name} must be contiguous")
 
 
-# Token batches up to this size run the fused GEMV (each tile decoded once per
-# up to 8 tokens); larger ones a tensor-core path.
-GEMV_MAX_BATCH = 8
+# Token batches up to this size run the fused GEMV, which decodes each tile once
+# for the whole batch; larger ones a tensor-core path. Measured on 28672 x 8192:
+# the GEMV's CUDA-core math for 8 tokens costs 2x its single-token time, more
+# than the tcgen05 kernel (1.3x) or decoding W to fp16 once for cuBLAS (1.35x).
+GEMV_MAX_BATCH = 4
 
 
 @dataclass
@@ -165,7 +167,7 @@ class DeviceMatrix:
     def matmul(self, x: torch.Tensor, scales: torch.Tensor, fused_max_batch: int = GEMV_MAX_BATCH) -> torch.Tensor:
         """y = x @ W^T for x [..., cols] fp16: the one dispatch every batched
         entry point uses. Up to `fused_max_batch` token rows run the fused
-        GEMV, which decodes each tile once for up to 8 tokens. Larger batches
+        GEMV, which decodes each tile once for the whole batch. Larger batches
         run the tcgen05 kernel (matmul_tc) when the tile layout has one (tile
         widths 128 and 256); otherwise W is decoded once to fp16
         (dequantize) for a tensor-core GEMM."""

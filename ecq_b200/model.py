@@ -305,8 +305,9 @@ class Llama7BDecoder:
             else:
                 o = lw["o"](att.reshape(1, L))
                 mk("gemv o")
-                o = self._all_reduce(o)
-                mk("nccl all-reduce")
+                if self.tp > 1:
+                    o = self._all_reduce(o)
+                    mk("nccl all-reduce")
                 a = self._add_rms(h, o, lw["ln2"])
                 mk("add + rmsnorm")
             gu = lw["gate_up"](a)                   # [1, 2F]: gate | up
@@ -321,8 +322,9 @@ class Llama7BDecoder:
             else:
                 d = lw["down"](m)
                 mk("gemv down")
-                d = self._all_reduce(d)
-                mk("nccl all-reduce")
+                if self.tp > 1:
+                    d = self._all_reduce(d)
+                    mk("nccl all-reduce")
         if pending:
             a = self.xch.add_rmsnorm(h, self.norm, cfg.eps)
             mk("exchange consumer: sum + add + rmsnorm")

@@ -94,8 +94,8 @@ def _(x, data, tile_offset, stream_len, dec_table, scales, workspace, status, ro
 
 def rans_matmul(x: torch.Tensor, m: DeviceMatrix, scales: torch.Tensor) -> torch.Tensor:
     """x [B, cols] fp16 -> y [B, rows], routed as DeviceMatrix.matmul routes:
-    up to GEMV_MAX_BATCH tokens the fused GEMV (each tile decoded once for up
-    to 8 tokens), more the tcgen05 kernel when the tile layout has one, else
+    up to GEMV_MAX_BATCH tokens the fused GEMV (each tile decoded once for the
+    batch), more the tcgen05 kernel when the tile layout has one, else
     W decoded once to fp16 for a tensor-core GEMM."""
     x2 = x.reshape(-1, m.cols)
     if x2.shape[0] <= GEMV_MAX_BATCH:

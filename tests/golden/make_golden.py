@@ -4,7 +4,7 @@ reference codec.
 
 Run from the repository root, in a container where the reference is mounted:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of a drxddy/ecq checkout>
 
 It imports the reference's own ``src/rans.py`` and ``src/interleaved_rans.py``
 (drxddy/ecq) and records, for seeded inputs, what they produce:
@@ -251,4 +251,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <path of a drxddy/ecq checkout>")
+    main(sys.argv[1])

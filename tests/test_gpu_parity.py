@@ -107,7 +107,7 @@ def test_gemv_deterministic_and_workspace_reusable():
     m.check()
     for y in ys[1:]:
         assert torch.equal(y, ys[0])
-    assert int(m.workspace[-(512 // 8) * 4:].count_nonzero()) == 0  # slab counters back at zero
+    assert int(m.workspace[:(512 // 8) * 4].count_nonzero()) == 0  # slab counters (first) back at zero
 
 
 def test_constant_matrix():
