@@ -106,9 +106,11 @@ def _decoder(rank, world, dev):
     ref = Llama7BDecoder(cfg, device=dev, tp=1, seed=5)
     l_ref = ref.step_logits(tok).float()
     dec = Llama7BDecoder(cfg, device=dev, tp=world, rank=rank, seed=5, exchange="peer")
-    # every TP size draws the same global KV cache and keeps its heads
+    # every TP size draws the same global KV cache and keeps its heads (the
+    # last slot holds the new token's K/V, which ref's step has written)
     nh = dec.local_heads
-    assert torch.equal(dec.kv, ref.kv[:, :, rank * nh:(rank + 1) * nh])
+    kv = cfg.kv_len
+    assert torch.equal(dec.kv[:, :, :, :kv], ref.kv[:, :, rank * nh:(rank + 1) * nh, :kv])
     try:
         l_peer = dec.step_logits(tok).float()
         dec.use_peer = False
