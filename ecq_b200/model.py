@@ -79,24 +79,32 @@ class ShardedLinear:
         return rans_gemv(x, self.m, self.scales)
 
 
-# A batch-1 GEMV whose shard has fewer tiles than the GPU has warps (about
-# 4.7K) waits on one tile's serial decode: narrower tiles shorten that chain
-# but cost per-tile overhead and compression. Measured on TP-8 shard shapes,
-# the best width is the widest one that still gives this many tiles.
-MIN_TILES = 2048
+# A batch-1 GEMV runs its tiles in rounds over the GPU's warp slots (one CTA of
+# up to 32 warps per SM), and each round waits on one tile's serial decode of
+# tile_cols / 4 symbols per lane plus a fixed per-tile cost. Narrow tiles
+# shorten the chain but add tiles (rounds) and per-tile overhead, and compress
+# worse. shard_tile_cols picks the width with the least modelled time,
+# ceil(tiles / warp slots) * (tile_cols / 4 + TILE_OVERHEAD); on the TP shard
+# shapes of the 7B layers and the sweep (1536..22016 rows x 512..11008 columns)
+# it picks the fastest measured width or one within 3 % of it.
+WARP_SLOTS = 148 * 32
+TILE_OVERHEAD = 40
 
 
-def shard_tile_cols(rows: int, cols: int, group: int = GROUP, min_tiles: int = MIN_TILES) -> int:
-    """Tile width for encoding one [rows, cols] shard: the widest of
-    512 / 256 / 128 columns compatible with cols and the group size that
-    gives at least `min_tiles` 8-row tiles (else the narrowest compatible)."""
+def shard_tile_cols(rows: int, cols: int, group: int = GROUP, warp_slots: int = WARP_SLOTS) -> int:
+    """Tile width (512 / 256 / 128 columns) for encoding one [rows, cols]
+    shard: of the widths compatible with cols and the group size, the one
+    with the least modelled decode time (ties: the widest)."""
     ok = [c for c in (512, 256, 128) if cols % c == 0 and (c % group == 0 if group < c else group % c == 0)]
     if not ok:
         raise ValueError(f"no tile width for {cols} columns, group {group}")
-    for c in ok:
-        if ((rows + 7) // 8) * (cols // c) >= min_tiles:
-            return c
-    return ok[-1]
+    slabs = (rows + 7) // 8
+
+    def cost(c):
+        tiles = slabs * (cols // c)
+        return ((tiles + warp_slots - 1) // warp_slots) * (c // 4 + TILE_OVERHEAD)
+
+    return min(ok, key=lambda c: (cost(c), -c))
 
 
 def _encode_shards(parts, table: RANSTable, tile_cols: int | None, device) -> ShardedLinear:
