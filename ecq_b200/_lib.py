@@ -48,6 +48,7 @@ EXPORTS = (
     "ecq_matrix_dequantize",
     "ecq_gemv_workspace_bytes",
     "ecq_gemv",
+    "ecq_gemv_fused",
     "ecq_gemv_noalloc",
     "ecq_plain4_gemv",
     "ecq_matmul_workspace_bytes",
@@ -85,6 +86,20 @@ class MatrixView(ctypes.Structure):
     ]
 
 
+EPI_ROPE_KV = 1
+EPI_SILU_MUL = 2
+
+
+class GemvEpilogue(ctypes.Structure):
+    """Mirror of ``ecq_gemv_epilogue``."""
+
+    _fields_ = [
+        ("kind", c_int32), ("part_rows", c_uint32), ("head_dim", c_uint32), ("reserved", c_uint32),
+        ("cache_head_stride", c_int64), ("cos_f16", c_void_p), ("sin_f16", c_void_p),
+        ("k_cache_f16", c_void_p), ("v_cache_f16", c_void_p),
+    ]
+
+
 class TPComm(ctypes.Structure):
     """Mirror of ``ecq_tp_comm`` (include/ecq_comm.h)."""
 
@@ -113,6 +128,7 @@ def _declare(L: ctypes.CDLL) -> None:
         "ecq_plain4_gemv": (c_int32, [P, P, P, P, c_uint32, c_uint32, c_uint32, c_uint32, P]),
         "ecq_gemv_workspace_bytes": (c_int64, [POINTER(MatrixView), c_uint32]),
         "ecq_gemv": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, c_int64, P, P]),
+        "ecq_gemv_fused": (c_int32, [POINTER(MatrixView), P, P, P, POINTER(GemvEpilogue), P, c_int64, P, P]),
         "ecq_gemv_noalloc": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, P]),
         "ecq_matmul_workspace_bytes": (c_int64, [POINTER(MatrixView), c_uint32]),
         "ecq_matmul": (c_int32, [POINTER(MatrixView), P, P, P, c_uint32, P, c_int64, P, P]),
@@ -170,4 +186,4 @@ def ptr(a) -> int:
     return a.ctypes.data
 
 
-__all__ = ["lib", "check", "ptr", "MatrixView", "TPComm", "EcqError", "EXPORTS", "c_uint16"]
+__all__ = ["lib", "check", "ptr", "MatrixView", "TPComm", "GemvEpilogue", "EcqError", "EXPORTS", "c_uint16"]

@@ -108,6 +108,14 @@ struct MatrixParams {
     uint8_t* tp_peer[ECQ_TP_MAX_RANKS];
     uint32_t* tp_epoch;  // this rank's epoch counter
     uint32_t tp_world, tp_rank, tp_nmax;
+    // fused epilogue of a batch-1 GEMV (ecq_gemv_fused; epi_kind 0 otherwise)
+    uint32_t epi_kind;
+    uint32_t epi_part_rows, epi_head_dim;
+    int64_t epi_cache_stride;
+    const __half* epi_cos;
+    const __half* epi_sin;
+    __half* epi_kc;
+    __half* epi_vc;
 };
 
 // what matrix_kernel does with the decoded symbols
@@ -178,6 +186,41 @@ __device__ __forceinline__ void tp_push_slab(const MatrixParams& p, uint32_t sla
     for (uint32_t q = 0; q < p.tp_world; ++q) st_relaxed_sys_u64(p.tp_peer[q] + off, v);
 }
 
+// A finished row's value through the fused epilogue (all lanes call it; the
+// lanes with `writer` set store). Rows 2i and 2i+1 of a slab sit in lanes
+// 2i and 2i+1 of the same 8-lane group, so a pair meets with one shuffle.
+//  ROPE_KV:  y = q | k | v, each part_rows rows (heads x head_dim); q and k
+//            rotate pairs (2i, 2i+1) by angle index i (cos, sin [head_dim/2]);
+//            the rotated k and the v rows also go to the KV-cache slot
+//            (head h at h * cache_stride). The arithmetic is ecq_rope_kv_f16's
+//            on the fp16-rounded GEMV outputs.
+//  SILU_MUL: rows interleave gate and up (row 2j gate j, 2j + 1 up j); y[j] =
+//            silu(gate j) * up j, the arithmetic of ecq_silu_mul_f16.
+__device__ __forceinline__ void gemv_epilogue(const MatrixParams& p, uint32_t slab, int row, bool writer, float s) {
+    const uint32_t r = slab * kTileRows + row;
+    const float v = __half2float(__float2half_rn(s));
+    const float pv = __shfl_xor_sync(0xffffffffu, v, 1);
+    if (p.epi_kind == ECQ_EPI_ROPE_KV) {
+        const uint32_t part = r / p.epi_part_rows, rr = r - part * p.epi_part_rows;
+        const uint32_t head = rr / p.epi_head_dim, d = rr - head * p.epi_head_dim;
+        __half out = __float2half_rn(v);
+        if (part < 2) {
+            const float c = __half2float(p.epi_cos[d >> 1]), sn = __half2float(p.epi_sin[d >> 1]);
+            out = (d & 1) ? __float2half_rn(pv * sn + v * c) : __float2half_rn(v * c - pv * sn);
+        }
+        if (writer) {
+            p.y[r] = out;
+            if (part == 1) p.epi_kc[head * p.epi_cache_stride + d] = out;
+            if (part == 2) p.epi_vc[head * p.epi_cache_stride + d] = out;
+        }
+    } else {  // ECQ_EPI_SILU_MUL
+        if (writer && !(row & 1)) {
+            const float g = __half2float(__float2half_rn(v / (1.f + __expf(-v))));
+            p.y[r >> 1] = __float2half_rn(g * pv);
+        }
+    }
+}
+
 __device__ __forceinline__ void complete_pending(const MatrixParams& p, PendingSlab& pend, int lane) {
     if (pend.slab == 0xffffffffu) return;
     const uint32_t old = __shfl_sync(0xffffffffu, pend.old, 0);
@@ -190,10 +233,12 @@ __device__ __forceinline__ void complete_pending(const MatrixParams& p, PendingS
         for (uint32_t k = kp; k < p.n_ktiles; k += 4) s += __ldcg(base + static_cast<size_t>(k) * kTileRows + row);
         s += __shfl_xor_sync(0xffffffffu, s, 8);
         s += __shfl_xor_sync(0xffffffffu, s, 16);
-        if (p.tp_world == 0) {
-            if (kp == 0 && row < pend.rows) p.y[slab * kTileRows + row] = __float2half_rn(s);
-        } else {
+        if (p.tp_world != 0) {
             tp_push_slab(p, slab, row, kp == 0 && row < pend.rows, s);
+        } else if (p.epi_kind != 0) {
+            gemv_epilogue(p, slab, row, kp == 0 && row < pend.rows, s);
+        } else {
+            if (kp == 0 && row < pend.rows) p.y[slab * kTileRows + row] = __float2half_rn(s);
         }
         if (lane == 0) p.slab_count[slab] = 0u;
     }
@@ -786,6 +831,7 @@ struct LaunchArgs {
     __half* w_out = nullptr;
     void* workspace = nullptr;
     const ecq_tp_comm* comm = nullptr;
+    const ecq_gemv_epilogue* epi = nullptr;
     uint32_t batch_here = 1;
 };
 
@@ -821,6 +867,16 @@ int32_t launch_matrix(const ecq_matrix_view* m, int mode, int nb, const LaunchAr
     if (mode == kModeGemv || mode == kModeGemvBatch) {
         p.slab_count = static_cast<uint32_t*>(la.workspace);
         p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(la.workspace) + ws_counter_bytes(m));
+    }
+    if (la.epi) {
+        p.epi_kind = static_cast<uint32_t>(la.epi->kind);
+        p.epi_part_rows = la.epi->part_rows;
+        p.epi_head_dim = la.epi->head_dim;
+        p.epi_cache_stride = la.epi->cache_head_stride;
+        p.epi_cos = static_cast<const __half*>(la.epi->cos_f16);
+        p.epi_sin = static_cast<const __half*>(la.epi->sin_f16);
+        p.epi_kc = static_cast<__half*>(la.epi->k_cache_f16);
+        p.epi_vc = static_cast<__half*>(la.epi->v_cache_f16);
     }
     if (la.comm) {
         p.tp_world = la.comm->world;
@@ -917,6 +973,30 @@ int32_t ecq_gemv(const ecq_matrix_view* m, const void* x_f16, const void* scales
         b += here;
     }
     return ECQ_OK;
+}
+
+int32_t ecq_gemv_fused(const ecq_matrix_view* m, const void* x_f16, const void* scales_f16, void* y_f16,
+                       const ecq_gemv_epilogue* epi, void* workspace, int64_t workspace_bytes, uint32_t* d_status,
+                       void* stream) {
+    if (!view_ok(m) || !x_f16 || !scales_f16 || !y_f16 || !epi || !d_status) return ECQ_ERR_ARG;
+    if (epi->kind == ECQ_EPI_ROPE_KV) {
+        if (epi->head_dim < 2 || (epi->head_dim & 1) || epi->part_rows == 0 || epi->part_rows % 8 ||
+            epi->part_rows % epi->head_dim || m->rows != 3 * epi->part_rows || !epi->cos_f16 || !epi->sin_f16 ||
+            !epi->k_cache_f16 || !epi->v_cache_f16 || epi->cache_head_stride < static_cast<int64_t>(epi->head_dim))
+            return ECQ_ERR_ARG;
+    } else if (epi->kind == ECQ_EPI_SILU_MUL) {
+        if (m->rows & 1) return ECQ_ERR_ARG;
+    } else {
+        return ECQ_ERR_ARG;
+    }
+    if (!workspace || workspace_bytes < ws_bytes(m, 1)) return ECQ_ERR_WORKSPACE;
+    LaunchArgs la;
+    la.x = static_cast<const __half*>(x_f16);
+    la.scales = static_cast<const __half*>(scales_f16);
+    la.y = static_cast<__half*>(y_f16);
+    la.workspace = workspace;
+    la.epi = epi;
+    return launch_matrix(m, kModeGemv, 1, la, d_status, static_cast<cudaStream_t>(stream));
 }
 
 int32_t ecq_gemv_tp(const ecq_matrix_view* m, const void* x_f16, const void* scales_f16, const ecq_tp_comm* comm,

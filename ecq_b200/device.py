@@ -212,6 +212,42 @@ class DeviceMatrix:
                              ptr(self.status), _stream_ptr(stream)), "gemv")
         return out[0] if squeeze else out
 
+    def gemv_rope_kv(self, x: torch.Tensor, scales: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                     k_slot: torch.Tensor, v_slot: torch.Tensor, head_dim: int, cache_head_stride: int,
+                     out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """Batch-1 GEMV of a fused q|k|v projection (rows = 3 * heads *
+        head_dim) with the rotary embedding and the KV-cache store fused in:
+        returns y = q | k | v with q and k rotated (pairs (2i, 2i+1) by angle
+        index i), and writes the rotated k and v into k_slot / v_slot (head h
+        at h * cache_head_stride)."""
+        epi = _lib.GemvEpilogue(kind=_lib.EPI_ROPE_KV, part_rows=self.rows // 3, head_dim=int(head_dim), reserved=0,
+                                cache_head_stride=int(cache_head_stride), cos_f16=ptr(cos), sin_f16=ptr(sin),
+                                k_cache_f16=ptr(k_slot), v_cache_f16=ptr(v_slot))
+        if out is None:
+            out = torch.empty(1, self.rows, dtype=torch.float16, device=self.device)
+        return self._gemv_fused(x, scales, epi, out, stream)
+
+    def gemv_silu_mul(self, x: torch.Tensor, scales: torch.Tensor, out: torch.Tensor | None = None,
+                      stream=None) -> torch.Tensor:
+        """Batch-1 GEMV of a projection whose rows interleave gate and up
+        (row 2j gate j, 2j+1 up j) with SwiGLU fused in: returns
+        silu(gate) * up [1, rows / 2]."""
+        epi = _lib.GemvEpilogue(kind=_lib.EPI_SILU_MUL)
+        if out is None:
+            out = torch.empty(1, self.rows // 2, dtype=torch.float16, device=self.device)
+        return self._gemv_fused(x, scales, epi, out, stream)
+
+    def _gemv_fused(self, x, scales, epi, out, stream):
+        x2 = x.reshape(1, self.cols)
+        if x2.dtype != torch.float16:
+            raise ValueError("x must be float16")
+        _require_cuda(x2, "x")
+        _require_cuda(scales, "scales")
+        _require_cuda(out, "out")
+        check(lib().ecq_gemv_fused(self.view(), ptr(x2), ptr(scales), ptr(out), epi, ptr(self.workspace),
+                                   self.workspace.numel(), ptr(self.status), _stream_ptr(stream)), "gemv_fused")
+        return out
+
     def read_status(self, reset: bool = True) -> int:
         """Synchronising read of the device status word (ECQ_STATUS_* bits)."""
         s = int(self.status.item())

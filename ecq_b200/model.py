@@ -18,8 +18,11 @@ Tensor parallelism (one process per GPU, NCCL over NVLink):
 Each matrix (q|k|v and gate|up as fused projections sharing one table) is
 encoded with its global table and every rank encodes exactly the tiles of its
 shard, which are the same tiles whatever the TP size. A layer launches 4
-fused GEMVs, 3 glue kernels (ecq_glue.h), attention and, with TP, 2
-all-reduces.
+fused GEMVs -- q|k|v with the rotary embedding and the KV-cache store fused
+into its epilogue, gate|up (rows interleaved) with SwiGLU fused in -- one
+residual add + RMSNorm before each of the two projections that read the
+residual stream (with TP > 1 these are the exchange consumers, the
+row-parallel sums fused into the GEMV push and the consumer) and attention.
 """
 from __future__ import annotations
 
@@ -180,8 +183,12 @@ class Llama7BDecoder:
             lw["o"] = _encode_shards([(W["o"][0], W["o"][1], (0, H), (kt_o[0] * tc_h, kt_o[1] * tc_h))],
                                      _table_of(W["o"][0]), None, self.dev)
             t_gu = _table_of(W["gate"][0], W["up"][0])
-            lw["gate_up"] = _encode_shards([(W[n][0], W[n][1], mr, (0, H)) for n in ("gate", "up")], t_gu, None,
-                                           self.dev)
+            # gate and up rows interleaved (row 2j gate j, 2j + 1 up j), so the
+            # GEMV's epilogue finds each pair in one row slab for SwiGLU
+            gu_q = torch.stack((W["gate"][0][mr[0]:mr[1]], W["up"][0][mr[0]:mr[1]]), dim=1).reshape(-1, H)
+            gu_s = torch.stack((W["gate"][1][mr[0]:mr[1]], W["up"][1][mr[0]:mr[1]]), dim=1).reshape(gu_q.shape[0], -1)
+            lw["gate_up"] = _encode_shards([(gu_q, gu_s, (0, gu_q.shape[0]), (0, H))], t_gu, None, self.dev)
+            del gu_q, gu_s
             lw["down"] = _encode_shards([(W["down"][0], W["down"][1], (0, H), (kt_d[0] * tc_m, kt_d[1] * tc_m))],
                                         _table_of(W["down"][0]), None, self.dev)
             del W
@@ -278,8 +285,6 @@ class Llama7BDecoder:
         cfg = self.cfg
         D, nh = cfg.head_dim, self.local_heads
         L = nh * D
-        F = self.mlp_rows[1] - self.mlp_rows[0]
-        stream = torch.cuda.current_stream(self.dev).cuda_stream
         mk = self._mark
         h = self.embed[token].reshape(1, cfg.hidden).clone()
         mk("embed")
@@ -293,14 +298,12 @@ class Llama7BDecoder:
             else:
                 a = self._add_rms(h, d, lw["ln1"])
                 mk("add + rmsnorm")
-            qkv = lw["qkv"](a)                      # [1, 3L]: q | k | v
-            mk("gemv q|k|v")
             kslot = self.kv[li, 0, :, cfg.kv_len]
             vslot = self.kv[li, 1, :, cfg.kv_len]
-            check(lib().ecq_rope_kv_f16(qkv.data_ptr(), qkv[:, L:].data_ptr(), qkv[:, 2 * L:].data_ptr(),
-                                        kslot.data_ptr(), vslot.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(),
-                                        nh, D, (cfg.kv_len + 1) * D, stream), "rope_kv")
-            mk("rope + kv write")
+            # [1, 3L]: q | k | v, q and k rotated, k and v stored into the cache slot
+            qkv = lw["qkv"].m.gemv_rope_kv(a, lw["qkv"].scales, self.cos, self.sin, kslot, vslot, D,
+                                           (cfg.kv_len + 1) * D)
+            mk("gemv q|k|v + rope + kv write")
             q = qkv[:, :L].reshape(1, nh, 1, D)
             att = torch.nn.functional.scaled_dot_product_attention(q, self.kv[li, 0].unsqueeze(0),
                                                                    self.kv[li, 1].unsqueeze(0))
@@ -318,11 +321,8 @@ class Llama7BDecoder:
                     mk("nccl all-reduce")
                 a = self._add_rms(h, o, lw["ln2"])
                 mk("add + rmsnorm")
-            gu = lw["gate_up"](a)                   # [1, 2F]: gate | up
-            mk("gemv gate|up")
-            m = torch.empty(1, F, device=self.dev, dtype=torch.float16)
-            check(lib().ecq_silu_mul_f16(gu.data_ptr(), m.data_ptr(), F, 1, stream), "silu_mul")
-            mk("silu * mul")
+            m = lw["gate_up"].m.gemv_silu_mul(a, lw["gate_up"].scales)  # [1, F] = silu(gate) * up
+            mk("gemv gate|up + silu * mul")
             if peer:
                 self.xch.gemv_push(lw["down"].m, m, lw["down"].scales)
                 mk("gemv down + push")

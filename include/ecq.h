@@ -197,6 +197,37 @@ int64_t ecq_gemv_workspace_bytes(const ecq_matrix_view *m, uint32_t batch);
 int32_t ecq_gemv(const ecq_matrix_view *m, const void *x_f16, const void *scales_f16, void *y_f16,
                  uint32_t batch, void *workspace, int64_t workspace_bytes, uint32_t *d_status, void *stream);
 
+/* Fused epilogues of a batch-1 GEMV (ecq_gemv_fused): the element-wise step
+ * that follows a projection in a transformer decode step, applied as each
+ * row of y is finished, so that it needs no kernel of its own. */
+#define ECQ_EPI_ROPE_KV 1   /* y = q | k | v: rotary embedding of q and k, k and v into the KV cache */
+#define ECQ_EPI_SILU_MUL 2  /* rows interleave gate and up: y[j] = silu(gate j) * up j */
+
+typedef struct ecq_gemv_epilogue {
+    int32_t kind;               /* ECQ_EPI_* */
+    uint32_t part_rows;         /* ROPE_KV: rows of each of q, k, v (heads * head_dim, a multiple of 8) */
+    uint32_t head_dim;          /* ROPE_KV: even */
+    uint32_t reserved;
+    int64_t cache_head_stride;  /* ROPE_KV: elements between heads in the cache slot */
+    const void *cos_f16;        /* ROPE_KV: [head_dim / 2] for the new token's position */
+    const void *sin_f16;
+    void *k_cache_f16;          /* ROPE_KV: the new token's slot, head h at h * cache_head_stride */
+    void *v_cache_f16;
+} ecq_gemv_epilogue;
+
+/* ecq_gemv at batch 1 with a fused epilogue. ROPE_KV (m->rows = 3 *
+ * part_rows): y holds q | k | v with q and k rotated pair by pair -- (2i,
+ * 2i+1) by angle index i within each head -- and the rotated k and v are
+ * also stored into the cache slot (the arithmetic of ecq_rope_kv_f16 on the
+ * fp16-rounded GEMV outputs). SILU_MUL (m->rows even, rows interleaving gate
+ * and up): y [rows / 2] = silu(gate) * up (the arithmetic of
+ * ecq_silu_mul_f16). Replaces a GEMV followed by ecq_rope_kv_f16 or
+ * ecq_silu_mul_f16 (the glue of the reference's MLX fork; model structure
+ * experiments/real_model_test.py:18-113). Workspace as ecq_gemv for batch 1. */
+int32_t ecq_gemv_fused(const ecq_matrix_view *m, const void *x_f16, const void *scales_f16, void *y_f16,
+                       const ecq_gemv_epilogue *epi, void *workspace, int64_t workspace_bytes, uint32_t *d_status,
+                       void *stream);
+
 /* Size of the scratch array ecq_gemv_noalloc uses (4 MiB per GPU). */
 #define ECQ_NOALLOC_SCRATCH_BYTES (4u << 20)
 
