@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true", help="skip the 8192x8192 entropy sweep")
     ap.add_argument("--no-sharded", action="store_true", help="skip the column-sharded sweep (N > 1)")
     ap.add_argument("--no-control", action="store_true", help="skip the plain 4-bit GEMV control")
+    ap.add_argument("--compression-table", action="store_true",
+                    help="print bits/symbol per tile shape against the entropy (host only, no GPU) and exit")
     return ap.parse_args()
 
 
@@ -1055,8 +1057,45 @@ def run_llama(args, world, rank, local, dev, barrier, max_ranks):
     return res
 
 
+def compression_table(M=4096, K=4096):
+    """Bits per symbol of the packed format against the symbols' entropy, per
+    tile shape: the kernels' 8-row tiles of 128, 256 and 512 columns (32
+    streams of tile_cols/4 symbols), and taller or wider tiles the format
+    allows but the kernels do not take (16x512, 8x1024, 32x512: 256-512
+    symbols per stream). The excess over the entropy is each stream's 4-byte
+    flush plus the padding of every stream to its tile's longest. Inputs: the
+    sweep's Laplace symbols at b = 0.3, 0.5, 1, 2 and Student-t(4) weights
+    quantised per group of 128, M x K each."""
+    from ecq_b200 import synthetic as syn
+    from ecq_b200.codec import RANSTable
+    from oracle import oracle
+
+    cases = [(f"laplace b={b}", syn.laplace_symbols(M, K, b=b, seed=1)) for b in (0.3, 0.5, 1.0, 2.0)]
+    cases.append(("student-t(4) group-128", syn.quantize_symmetric_groups(
+        syn.student_t_weights(M, K, seed=2).astype(np.float32), 128)[0]))
+    rows = []
+    for name, sym in cases:
+        p_ = np.bincount(sym.reshape(-1), minlength=16) / sym.size
+        ent = float(-(p_[p_ > 0] * np.log2(p_[p_ > 0])).sum())
+        table = RANSTable.from_symbols(sym)
+        row = {"symbols": name, "entropy_bits": round(ent, 3)}
+        for tr, tc in ((8, 128), (8, 256), (8, 512), (16, 512), (8, 1024), (32, 512)):
+            nbytes = 0
+            for r0 in range(0, M, tr):
+                for c0 in range(0, K, tc):
+                    data, _, _ = oracle.encode_interleaved(sym[r0:r0 + tr, c0:c0 + tc].reshape(-1), table.freq, 32)
+                    nbytes += data.size
+            row[f"{tr}x{tc}"] = round(8.0 * nbytes / sym.size, 4)
+        rows.append(row)
+    return {"shape": [M, K], "streams_per_tile": 32, "bits_per_symbol": rows,
+            "kernels_take": ["8x128", "8x256", "8x512"]}
+
+
 def main():
     args = parse()
+    if args.compression_table:
+        print(json.dumps(compression_table()), flush=True)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
