@@ -66,6 +66,9 @@ EXPORTS = (
     "ecq_add_rmsnorm_f16",
     "ecq_rope_kv_f16",
     "ecq_silu_mul_f16",
+    "ecq_decode_attention_workspace_bytes",
+    "ecq_decode_attention_splits",
+    "ecq_decode_attention_f16",
 )
 
 
@@ -145,6 +148,9 @@ def _declare(L: ctypes.CDLL) -> None:
         "ecq_add_rmsnorm_f16": (c_int32, [P, P, P, P, P, c_int32, c_int32, ctypes.c_float, P]),
         "ecq_rope_kv_f16": (c_int32, [P, P, P, P, P, P, P, c_int32, c_int32, c_int64, P]),
         "ecq_silu_mul_f16": (c_int32, [P, P, c_int32, c_int32, P]),
+        "ecq_decode_attention_workspace_bytes": (c_int64, [c_int32, c_int32]),
+        "ecq_decode_attention_splits": (c_int32, [c_int32, c_int32]),
+        "ecq_decode_attention_f16": (c_int32, [P, P, P, P, c_int32, c_int32, c_int32, c_int64, c_int32, P, c_int64, P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)

@@ -21,7 +21,7 @@ INCLUDE = ROOT / "include"
 OUT_DIR = PKG / "_lib"
 LIB = OUT_DIR / "libecq.so"
 
-SOURCES = ["ecq_device.cu", "ecq_matmul.cu", "ecq_plain4.cu", "ecq_comm.cu", "ecq_glue.cu", "ecq_host.cpp"]
+SOURCES = ["ecq_device.cu", "ecq_matmul.cu", "ecq_plain4.cu", "ecq_comm.cu", "ecq_glue.cu", "ecq_attention.cu", "ecq_host.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

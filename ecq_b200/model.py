@@ -138,10 +138,15 @@ class Llama7BDecoder:
     rank of a tensor-parallel group (tp = world size, rank = this rank)."""
 
     def __init__(self, cfg: Llama7BConfig | None = None, device=None, tp: int = 1, rank: int = 0, seed: int = 3,
-                 group=None, exchange: str = "peer"):
+                 group=None, exchange: str = "peer", attention: str = "ecq"):
         """exchange (tp > 1): "peer" fuses each row-parallel layer's all-reduce
         into its GEMV and the next add + RMSNorm over NVLink peer memory
-        (ecq_b200.comm); "nccl" runs GEMV -> NCCL all-reduce -> add + RMSNorm."""
+        (ecq_b200.comm); "nccl" runs GEMV -> NCCL all-reduce -> add + RMSNorm.
+        attention: "ecq" runs libecq's split-key decode attention
+        (ecq_decode_attention_f16), "sdpa" torch's scaled_dot_product_attention."""
+        if attention not in ("ecq", "sdpa"):
+            raise ValueError("attention is 'ecq' or 'sdpa'")
+        self.attention = attention
         self.cfg = cfg = cfg or Llama7BConfig()
         self.dev = torch.device(device or "cuda")
         self.tp, self.rank, self.group = tp, rank, group
@@ -226,6 +231,11 @@ class Llama7BDecoder:
         self.logits = torch.empty(tp, max(self.vocab_sizes), device=self.dev, dtype=torch.float16)
         self.xch = None
         self._marks = None  # CUDA events of a step_breakdown run
+        keys = cfg.kv_len + 1
+        self.att_splits = int(lib().ecq_decode_attention_splits(self.local_heads, keys))
+        self.att_ws = torch.zeros(int(lib().ecq_decode_attention_workspace_bytes(self.local_heads, self.att_splits)),
+                                  dtype=torch.uint8, device=self.dev)
+        self.att_out = torch.empty(1, self.local_heads * D, dtype=torch.float16, device=self.dev)
         self.use_peer = True  # with an exchange: False runs the NCCL path instead (same weights)
         if self.exchange == "peer":
             from .comm import PeerExchange
@@ -304,10 +314,20 @@ class Llama7BDecoder:
             qkv = lw["qkv"].m.gemv_rope_kv(a, lw["qkv"].scales, self.cos, self.sin, kslot, vslot, D,
                                            (cfg.kv_len + 1) * D)
             mk("gemv q|k|v + rope + kv write")
-            q = qkv[:, :L].reshape(1, nh, 1, D)
-            att = torch.nn.functional.scaled_dot_product_attention(q, self.kv[li, 0].unsqueeze(0),
-                                                                   self.kv[li, 1].unsqueeze(0))
-            mk("attention (sdpa)")
+            if self.attention == "ecq":
+                att = self.att_out
+                check(lib().ecq_decode_attention_f16(qkv.data_ptr(), self.kv[li, 0].data_ptr(),
+                                                     self.kv[li, 1].data_ptr(), att.data_ptr(), nh, D,
+                                                     cfg.kv_len + 1, (cfg.kv_len + 1) * D, self.att_splits,
+                                                     self.att_ws.data_ptr(), self.att_ws.numel(),
+                                                     torch.cuda.current_stream(self.dev).cuda_stream),
+                      "decode attention")
+                mk("attention (ecq split-key)")
+            else:
+                q = qkv[:, :L].reshape(1, nh, 1, D)
+                att = torch.nn.functional.scaled_dot_product_attention(q, self.kv[li, 0].unsqueeze(0),
+                                                                       self.kv[li, 1].unsqueeze(0))
+                mk("attention (sdpa)")
             if peer:
                 self.xch.gemv_push(lw["o"].m, att.reshape(1, L).contiguous(), lw["o"].scales)
                 mk("gemv o + push")

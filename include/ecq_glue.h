@@ -32,6 +32,22 @@ int32_t ecq_rope_kv_f16(void *q, const void *k, const void *v, void *k_cache, vo
  * (gate in the first f columns, up in the next f). */
 int32_t ecq_silu_mul_f16(const void *gate_up, void *m, int32_t f, int32_t rows, void *stream);
 
+/* Batch-1 decode attention: out[h] = softmax(q[h] . K[h]^T / sqrt(head_dim))
+ * . V[h] for heads h < heads over keys t < keys, fp16 in/out, fp32 softmax
+ * and accumulation (flash-decoding: the keys split over `splits` CTAs per
+ * head, the last CTA of each head merging the partial results in split
+ * order, so the result is deterministic). q and out are [heads, head_dim];
+ * key t of head h is at k_cache + h * head_stride + t * head_dim (same for
+ * v_cache). head_dim must be 128; pointers 8-byte aligned. The workspace
+ * (ecq_decode_attention_workspace_bytes) must be zero-filled once; each call
+ * leaves its counters zero again. ecq_decode_attention_splits gives a split
+ * count that puts about two CTAs per SM. */
+int64_t ecq_decode_attention_workspace_bytes(int32_t heads, int32_t splits);
+int32_t ecq_decode_attention_splits(int32_t heads, int32_t keys);
+int32_t ecq_decode_attention_f16(const void *q, const void *k_cache, const void *v_cache, void *out, int32_t heads,
+                                 int32_t head_dim, int32_t keys, int64_t head_stride, int32_t splits, void *workspace,
+                                 int64_t workspace_bytes, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
