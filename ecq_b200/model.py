@@ -90,6 +90,10 @@ class ShardedLinear:
 # ceil(tiles / warp slots) * (tile_cols / 4 + TILE_OVERHEAD); on the TP shard
 # shapes of the 7B layers and the sweep (1536..22016 rows x 512..11008 columns)
 # it picks the fastest measured width or one within 3 % of it.
+# Heads per rank up to which the split-key decode attention beats cuDNN's
+# SDPA (2049 keys, head_dim 128, in a CUDA graph).
+ECQ_ATTENTION_MAX_HEADS = 8
+
 WARP_SLOTS = 148 * 32
 TILE_OVERHEAD = 40
 
@@ -138,16 +142,20 @@ class Llama7BDecoder:
     rank of a tensor-parallel group (tp = world size, rank = this rank)."""
 
     def __init__(self, cfg: Llama7BConfig | None = None, device=None, tp: int = 1, rank: int = 0, seed: int = 3,
-                 group=None, exchange: str = "peer", attention: str = "ecq"):
+                 group=None, exchange: str = "peer", attention: str = "auto"):
         """exchange (tp > 1): "peer" fuses each row-parallel layer's all-reduce
         into its GEMV and the next add + RMSNorm over NVLink peer memory
         (ecq_b200.comm); "nccl" runs GEMV -> NCCL all-reduce -> add + RMSNorm.
         attention: "ecq" runs libecq's split-key decode attention
-        (ecq_decode_attention_f16), "sdpa" torch's scaled_dot_product_attention."""
-        if attention not in ("ecq", "sdpa"):
-            raise ValueError("attention is 'ecq' or 'sdpa'")
-        self.attention = attention
+        (ecq_decode_attention_f16), "sdpa" torch's scaled_dot_product_attention,
+        "auto" the first for at most ECQ_ATTENTION_MAX_HEADS heads per rank
+        (where it was measured faster), the second above."""
         self.cfg = cfg = cfg or Llama7BConfig()
+        if attention not in ("ecq", "sdpa", "auto"):
+            raise ValueError("attention is 'ecq', 'sdpa' or 'auto'")
+        if attention == "auto":
+            attention = "ecq" if cfg.heads // tp <= ECQ_ATTENTION_MAX_HEADS else "sdpa"
+        self.attention = attention
         self.dev = torch.device(device or "cuda")
         self.tp, self.rank, self.group = tp, rank, group
         if exchange not in ("peer", "nccl"):
