@@ -11,7 +11,7 @@
 //     online softmax (running max m, sum l, output o[4]) in fp32 with exp2.
 //   * the 4 warps merge in shared memory; the CTA writes its (m, l, o[D]) to
 //     the workspace and counts itself in the head's counter. The CTA that
-//     counts last merges the S partials in split order (deterministic) and
+//     counts last merges the S partials in a fixed order (deterministic) and
 //     writes att[h] in fp16, then clears the counter for the next call.
 // The arithmetic follows flash-decoding (fp32 softmax and accumulation over
 // fp16 K/V); results agree with cuDNN's SDPA to fp16 rounding.
@@ -31,6 +31,8 @@ using ecq_dev::pdl_wait;
 constexpr int kD = 128;
 constexpr int kWarps = 4;
 constexpr int kKeysPerStep = 8;
+constexpr int kMaxSplits = 128;
+constexpr int kStride = kD + 4;  // per partial: m, l, 2 pad, o[kD] (o 16-byte aligned)
 
 __device__ __forceinline__ uint2 ldg8(const __half* p) {
     uint2 v;
@@ -46,7 +48,7 @@ __device__ __forceinline__ void h4(uint2 v, float (&f)[4]) {
     f[3] = b.y;
 }
 
-// workspace per (head, split): m, l, o[kD] as floats; then one u32 counter per head
+// workspace per (head, split): m, l, 2 pad, o[kD] as floats; then one u32 counter per head
 __global__ void __launch_bounds__(kWarps * 32) decode_attention_kernel(const __half* __restrict__ q,
                                                                       const __half* __restrict__ kc,
                                                                       const __half* __restrict__ vc,
@@ -61,8 +63,8 @@ __global__ void __launch_bounds__(kWarps * 32) decode_attention_kernel(const __h
     const int chunk = (T + S - 1) / S;
     const int t0 = s * chunk, t1 = min(T, t0 + chunk);
     const int H = gridDim.x;
-    float* part = ws + (static_cast<size_t>(h) * S + s) * (kD + 2);
-    uint32_t* counter = reinterpret_cast<uint32_t*>(ws + static_cast<size_t>(H) * S * (kD + 2)) + h;
+    float* part = ws + (static_cast<size_t>(h) * S + s) * kStride;
+    uint32_t* counter = reinterpret_cast<uint32_t*>(ws + static_cast<size_t>(H) * S * kStride) + h;
 
     pdl_launch_dependents();
     pdl_wait();  // q and the new token's K/V come from the kernels before this one
@@ -140,25 +142,55 @@ __global__ void __launch_bounds__(kWarps * 32) decode_attention_kernel(const __h
             part[1] = L;
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) part[2 + 4 * lane + i] = O[i];
+        for (int i = 0; i < 4; ++i) part[4 + 4 * lane + i] = O[i];
         __threadfence();
         __syncwarp();
         if (lane == 0) s_last = (atomicAdd(counter, 1u) == static_cast<uint32_t>(S - 1)) ? 1u : 0u;
         __syncwarp();
         if (__shfl_sync(0xffffffffu, s_last, 0)) {
-            // the last split of this head merges all S partials in split order
+            // the last split of this head merges all S partials in a fixed
+            // order: lane j loads the (m, l) of splits j, j + 32, ... at once,
+            // the weights are summed by a fixed butterfly, and the outputs
+            // stream in split order
             __threadfence();
-            const float* hp = ws + static_cast<size_t>(h) * S * (kD + 2);
+            const float* hp = ws + static_cast<size_t>(h) * S * kStride;
+            float mk[kMaxSplits / 32], lk[kMaxSplits / 32];
             float MM = -INFINITY;
-            for (int k = 0; k < S; ++k) MM = fmaxf(MM, __ldcg(hp + static_cast<size_t>(k) * (kD + 2)));
-            float LL = 0.f, OO[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int k = 0; k < S; ++k) {
-                const float* pk = hp + static_cast<size_t>(k) * (kD + 2);
-                const float mk = __ldcg(pk);
-                const float a = (mk == -INFINITY) ? 0.f : exp2f(mk - MM);
-                LL = fmaf(a, __ldcg(pk + 1), LL);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) OO[i] = fmaf(a, __ldcg(pk + 2 + 4 * lane + i), OO[i]);
+            for (int u = 0; u < kMaxSplits / 32; ++u) {
+                const int k = lane + 32 * u;
+                mk[u] = k < S ? __ldcg(hp + static_cast<size_t>(k) * kStride) : -INFINITY;
+                lk[u] = k < S ? __ldcg(hp + static_cast<size_t>(k) * kStride + 1) : 0.f;
+                MM = fmaxf(MM, mk[u]);
+            }
+#pragma unroll
+            for (int off = 16; off; off >>= 1) MM = fmaxf(MM, __shfl_xor_sync(0xffffffffu, MM, off));
+            float ak[kMaxSplits / 32];
+            float LL = 0.f;
+#pragma unroll
+            for (int u = 0; u < kMaxSplits / 32; ++u) {
+                ak[u] = (mk[u] == -INFINITY) ? 0.f : exp2f(mk[u] - MM);
+                LL = fmaf(ak[u], lk[u], LL);
+            }
+#pragma unroll
+            for (int off = 16; off; off >>= 1) LL += __shfl_xor_sync(0xffffffffu, LL, off);
+            float OO[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int u = 0; u < kMaxSplits / 32; ++u) {
+                if (32 * u >= S) break;
+#pragma unroll 4
+                for (int j = 0; j < 32; ++j) {
+                    const int k = 32 * u + j;
+                    const float a = __shfl_sync(0xffffffffu, ak[u], j);
+                    if (k < S) {
+                        const float4 ov =
+                            __ldcg(reinterpret_cast<const float4*>(hp + static_cast<size_t>(k) * kStride + 4) + lane);
+                        OO[0] = fmaf(a, ov.x, OO[0]);
+                        OO[1] = fmaf(a, ov.y, OO[1]);
+                        OO[2] = fmaf(a, ov.z, OO[2]);
+                        OO[3] = fmaf(a, ov.w, OO[3]);
+                    }
+                }
             }
             const float inv = 1.f / LL;
             __half2* dst = reinterpret_cast<__half2*>(out + static_cast<size_t>(h) * kD + 4 * lane);
@@ -175,7 +207,7 @@ extern "C" {
 
 int64_t ecq_decode_attention_workspace_bytes(int32_t heads, int32_t splits) {
     if (heads < 1 || splits < 1) return -1;
-    return static_cast<int64_t>(heads) * splits * (kD + 2) * 4 + static_cast<int64_t>(heads) * 4;
+    return static_cast<int64_t>(heads) * splits * kStride * 4 + static_cast<int64_t>(heads) * 4;
 }
 
 int32_t ecq_decode_attention_splits(int32_t heads, int32_t keys) {
@@ -195,6 +227,7 @@ int32_t ecq_decode_attention_f16(const void* q, const void* k_cache, const void*
     if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
          reinterpret_cast<uintptr_t>(out)) & 7u)
         return -1;
+    if (splits > kMaxSplits) return -1;
     if (workspace_bytes < ecq_decode_attention_workspace_bytes(heads, splits)) return -9;
     const float qscale = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
     const cudaError_t rc = launch_pdl(decode_attention_kernel, dim3(heads, splits), dim3(kWarps * 32), 0,

@@ -61,64 +61,38 @@ __device__ __forceinline__ float sum_ranks(const uint64_t* slot, const ecq_tp_co
     return d;
 }
 
-// Exchange-buffer header words (include/ecq_comm.h): the epoch, the count of
-// consumer CTAs that have read the current epoch's slots, the count of CTAs
-// that have published their sum of squares, and the per-CTA sums of squares.
-struct Header {
-    uint32_t* epoch;
-    uint32_t* done;
-    uint32_t* arrived;
-    float* part;
-};
-__device__ __forceinline__ Header header(const ecq_tp_comm& c) {
-    uint8_t* b = static_cast<uint8_t*>(c.local);
-    return {reinterpret_cast<uint32_t*>(b), reinterpret_cast<uint32_t*>(b + 4), reinterpret_cast<uint32_t*>(b + 8),
-            reinterpret_cast<float*>(b + 128)};
-}
-__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* addr) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-    return v;
-}
+using ecq_dev::cluster_rank;
+using ecq_dev::cluster_size;
+using ecq_dev::cluster_sync;
+using ecq_dev::launch_pdl_cluster;
+using ecq_dev::ld_cluster_f32;
 
-// The last consumer CTA to finish reading advances the epoch (after clearing
-// the counters), so that no CTA can see the next epoch before every CTA has
-// read this one's slots. Called by thread 0 after a __syncthreads.
-__device__ __forceinline__ void finish_exchange(const Header& hd, uint32_t e) {
-    __threadfence();
-    const uint32_t prev = atomicAdd(hd.done, 1u);
-    if (prev == gridDim.x - 1) {
-        *reinterpret_cast<volatile uint32_t*>(hd.arrived) = 0u;
-        *reinterpret_cast<volatile uint32_t*>(hd.done) = 0u;
-        __threadfence();
-        *reinterpret_cast<volatile uint32_t*>(hd.epoch) = e + 1u;
-    }
-}
+// The consumers run as ONE thread-block cluster of kCluster CTAs: CTA rank r
+// owns the r-th contiguous chunk of the n elements. Cross-CTA steps use the
+// hardware cluster barrier and distributed shared memory, not global atomics
+// or spin waits: the RMSNorm's sum of squares is each CTA's partial in its
+// shared memory, read by every CTA in rank order (deterministic), and after a
+// final barrier -- every CTA has read its slots and every partial -- rank 0
+// advances the epoch.
+constexpr int kCluster = 8;
+constexpr int kConsumerThreads = 256;
 
-// Multi-CTA: sum every rank's partials of this rank's epoch e in rank order --
-// each slot is polled until its epoch half reads e + 1 (bounded: after ~1 s
-// the kernel sets ECQ_STATUS_TIMEOUT and stops waiting) -- then
-// h_out = h + d and y = rmsnorm(h_out) * w (the arithmetic of
-// ecq_add_rmsnorm_f16). Each CTA owns a contiguous chunk of the n elements;
-// the row's sum of squares is the sum of the CTAs' partial sums, published in
-// the exchange buffer's header and added in CTA order by every CTA after all
-// have arrived (a bounded wait; the grid is at most kMaxConsumerCtas CTAs,
-// which fit on the GPU at once), so y does not depend on CTA timing. The last
-// CTA to finish advances the epoch.
-__global__ void tp_add_rmsnorm_kernel(const __half* h, ecq_tp_comm c, const __half* __restrict__ w,
-                                      __half* h_out, __half* __restrict__ y, int n, float eps,
-                                      uint32_t* __restrict__ status) {
-    extern __shared__ float buf[];  // this CTA's chunk + 32 partials
+__global__ void __launch_bounds__(kConsumerThreads) tp_add_rmsnorm_kernel(const __half* h, ecq_tp_comm c,
+                                                                          const __half* __restrict__ w, __half* h_out,
+                                                                          __half* __restrict__ y, int n, float eps,
+                                                                          uint32_t* __restrict__ status) {
+    extern __shared__ float buf[];  // this CTA's chunk + 32 warp partials
     __shared__ uint32_t s_epoch, s_gave_up;
-    __shared__ float s_total;
-    const Header hd = header(c);
-    const int chunk = (n + gridDim.x - 1) / gridDim.x;
-    const int i0 = blockIdx.x * chunk;
+    __shared__ float s_part;
+    uint32_t* epoch = static_cast<uint32_t*>(c.local);
+    const uint32_t cr = cluster_rank(), cn = cluster_size();
+    const int chunk = (n + static_cast<int>(cn) - 1) / static_cast<int>(cn);
+    const int i0 = static_cast<int>(cr) * chunk;
     const int i1 = min(n, i0 + chunk);
     pdl_launch_dependents();
     pdl_wait();  // h and this rank's epoch come from the kernels before this one
     if (threadIdx.x == 0) {
-        s_epoch = *reinterpret_cast<volatile uint32_t*>(hd.epoch);
+        s_epoch = *reinterpret_cast<volatile uint32_t*>(epoch);
         s_gave_up = 0u;
     }
     __syncthreads();
@@ -141,42 +115,31 @@ __global__ void tp_add_rmsnorm_kernel(const __half* h, ecq_tp_comm c, const __ha
     if (threadIdx.x < 32) {
         float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
         for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (threadIdx.x == 0) {
-            // publish this CTA's sum of squares, then wait for every CTA's
-            *reinterpret_cast<volatile float*>(hd.part + blockIdx.x) = v;
-            __threadfence();
-            atomicAdd(hd.arrived, 1u);
-            const uint64_t t1 = global_timer_ns();
-            while (ld_acquire_gpu_u32(hd.arrived) < gridDim.x) {
-                if (global_timer_ns() - t1 > kFlagWaitNs) {
-                    atomicOr(status, ECQ_STATUS_TIMEOUT);
-                    break;
-                }
-            }
-            float tot = 0.f;
-            for (uint32_t b = 0; b < gridDim.x; ++b) tot += *reinterpret_cast<volatile float*>(hd.part + b);
-            s_total = tot;
-        }
+        if (threadIdx.x == 0) s_part = v;
     }
-    __syncthreads();
-    const float rs = rsqrtf(s_total / n + eps);
+    cluster_sync();  // every CTA's partial sum of squares is in its shared memory
+    float tot = 0.f;
+    for (uint32_t r = 0; r < cn; ++r) tot += ld_cluster_f32(&s_part, r);
+    const float rs = rsqrtf(tot / n + eps);
     for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x)
         y[i] = __hmul(__float2half_rn(buf[i - i0] * rs), w[i]);
-    __syncthreads();  // every slot and partial of this CTA has been read
-    if (threadIdx.x == 0) finish_exchange(hd, e);
+    cluster_sync();  // every slot and every partial has been read
+    if (cr == 0 && threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(epoch) = e + 1u;
 }
 
-// Multi-CTA: y[i] = sum over ranks of this rank's epoch-e slots (rank order,
-// fp32, rounded once to fp16), waiting for each slot as above; the last CTA
-// to finish advances the epoch. The plain all-reduce that closes a
-// column-sharded GEMV.
-__global__ void tp_sum_kernel(ecq_tp_comm c, __half* __restrict__ y, int n, uint32_t* __restrict__ status) {
+// y[i] = sum over ranks of this rank's epoch-e slots (rank order, fp32,
+// rounded once to fp16), waiting for each slot as above; one cluster, rank 0
+// advances the epoch after the final barrier. The plain all-reduce that
+// closes a column-sharded GEMV.
+__global__ void __launch_bounds__(kConsumerThreads) tp_sum_kernel(ecq_tp_comm c, __half* __restrict__ y, int n,
+                                                                  uint32_t* __restrict__ status) {
     __shared__ uint32_t s_epoch, s_gave_up;
-    const Header hd = header(c);
+    uint32_t* epoch = static_cast<uint32_t*>(c.local);
+    const uint32_t cr = cluster_rank(), cn = cluster_size();
     pdl_launch_dependents();
     pdl_wait();
     if (threadIdx.x == 0) {
-        s_epoch = *reinterpret_cast<volatile uint32_t*>(hd.epoch);
+        s_epoch = *reinterpret_cast<volatile uint32_t*>(epoch);
         s_gave_up = 0u;
     }
     __syncthreads();
@@ -184,18 +147,13 @@ __global__ void tp_sum_kernel(ecq_tp_comm c, __half* __restrict__ y, int n, uint
     const uint64_t* slot = reinterpret_cast<const uint64_t*>(static_cast<const uint8_t*>(c.local) + 256u) +
                            static_cast<size_t>(e & 1u) * c.world * c.n_max;
     const uint64_t t0 = global_timer_ns();
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    for (int i = static_cast<int>(cr * blockDim.x + threadIdx.x); i < n; i += static_cast<int>(cn * blockDim.x)) {
         const float d = sum_ranks(slot, c, i, e + 1u, t0, &s_gave_up, status);
         y[i] = __float2half_rn(d);
     }
-    __syncthreads();  // every slot of this CTA has been read
-    if (threadIdx.x == 0) finish_exchange(hd, e);
+    cluster_sync();  // every slot of every CTA has been read
+    if (cr == 0 && threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(epoch) = e + 1u;
 }
-
-constexpr int kConsumerThreads = 256;
-constexpr int kMaxConsumerCtas = 32;  // the header holds 32 partial sums of squares
-
-int consumer_ctas(int n) { return std::min(kMaxConsumerCtas, std::max(1, (n + kConsumerThreads - 1) / kConsumerThreads)); }
 
 bool comm_ok(const ecq_tp_comm* c) {
     if (!c || c->world < 1 || c->world > ECQ_TP_MAX_RANKS || c->rank >= c->world || !c->local) return false;
@@ -256,14 +214,15 @@ int32_t ecq_ipc_close(void* d_mapped) {
 
 int32_t ecq_tp_add_rmsnorm_f16(const void* h, const ecq_tp_comm* comm, const void* w, void* h_out, void* y, int32_t n,
                                float eps, uint32_t* d_status, void* stream) {
-    if (!h || !w || !h_out || !y || !d_status || !comm_ok(comm) || n < 1 || n > 32 * 12256 ||
+    if (!h || !w || !h_out || !y || !d_status || !comm_ok(comm) || n < 1 || n > kCluster * 12256 ||
         static_cast<uint32_t>(n) > comm->n_max)
         return ECQ_ERR_ARG;
-    const int ctas = consumer_ctas(n);
-    const int chunk = (n + ctas - 1) / ctas;
-    const cudaError_t rc = launch_pdl(tp_add_rmsnorm_kernel, dim3(ctas), dim3(kConsumerThreads),
-                                      (chunk + 32) * sizeof(float),
-                                      static_cast<cudaStream_t>(stream), static_cast<const __half*>(h), *comm,
+    const int chunk = (n + kCluster - 1) / kCluster;
+    if (!ecq_dev::ensure_smem_limit(reinterpret_cast<const void*>(tp_add_rmsnorm_kernel), (chunk + 32) * 4))
+        return ECQ_ERR_CUDA;
+    const cudaError_t rc = launch_pdl_cluster(tp_add_rmsnorm_kernel, dim3(kCluster), dim3(kConsumerThreads),
+                                              (chunk + 32) * sizeof(float), static_cast<cudaStream_t>(stream),
+                                              kCluster, static_cast<const __half*>(h), *comm,
                                       static_cast<const __half*>(w), static_cast<__half*>(h_out),
                                       static_cast<__half*>(y), n, eps, d_status);
     if (rc != cudaSuccess) {
@@ -275,9 +234,9 @@ int32_t ecq_tp_add_rmsnorm_f16(const void* h, const ecq_tp_comm* comm, const voi
 
 int32_t ecq_tp_sum_f16(const ecq_tp_comm* comm, void* y, int32_t n, uint32_t* d_status, void* stream) {
     if (!y || !d_status || !comm_ok(comm) || n < 1 || static_cast<uint32_t>(n) > comm->n_max) return ECQ_ERR_ARG;
-    const cudaError_t rc = launch_pdl(tp_sum_kernel, dim3(consumer_ctas(n)), dim3(kConsumerThreads), 0,
-                                      static_cast<cudaStream_t>(stream), *comm,
-                                      static_cast<__half*>(y), n, d_status);
+    const cudaError_t rc = launch_pdl_cluster(tp_sum_kernel, dim3(kCluster), dim3(kConsumerThreads), 0,
+                                              static_cast<cudaStream_t>(stream), kCluster, *comm,
+                                              static_cast<__half*>(y), n, d_status);
     if (rc != cudaSuccess) {
         cudaGetLastError();
         return ECQ_ERR_CUDA;

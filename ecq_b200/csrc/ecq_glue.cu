@@ -54,6 +54,52 @@ __global__ void add_rmsnorm_kernel(const __half* __restrict__ h, const __half* _
     }
 }
 
+// One row on one thread-block cluster of kRowCluster CTAs: CTA rank r takes
+// the r-th chunk of the row; the sum of squares is each CTA's partial in its
+// shared memory, read by every CTA in rank order after the cluster barrier
+// (deterministic, no global atomics).
+constexpr int kRowCluster = 8;
+constexpr int kRowThreads = 256;
+
+__global__ void __launch_bounds__(kRowThreads) add_rmsnorm_row_cluster_kernel(
+    const __half* h, const __half* __restrict__ d, const __half* __restrict__ w, __half* h_out,
+    __half* __restrict__ y, int n, float eps) {
+    extern __shared__ float buf[];  // this CTA's chunk + 32 warp partials (h_out may be h)
+    __shared__ float s_part;
+    const uint32_t cr = ecq_dev::cluster_rank(), cn = ecq_dev::cluster_size();
+    const int chunk = (n + static_cast<int>(cn) - 1) / static_cast<int>(cn);
+    const int i0 = static_cast<int>(cr) * chunk;
+    const int i1 = min(n, i0 + chunk);
+    pdl_launch_dependents();
+    pdl_wait();  // h and d come from the kernels before this one
+    float ss = 0.f;
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        float v = __half2float(h[i]);
+        if (d) v = __half2float(__float2half_rn(v + __half2float(d[i])));  // the residual is stored in fp16
+        buf[i - i0] = v;
+        ss += v * v;
+    }
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    float* part = buf + chunk;
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) s_part = v;
+    }
+    ecq_dev::cluster_sync();
+    float tot = 0.f;
+    for (uint32_t r = 0; r < cn; ++r) tot += ecq_dev::ld_cluster_f32(&s_part, r);
+    const float rs = rsqrtf(tot / n + eps);
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        const float v = buf[i - i0];
+        if (d) h_out[i] = __float2half_rn(v);
+        y[i] = __hmul(__float2half_rn(v * rs), w[i]);
+    }
+    ecq_dev::cluster_sync();  // no CTA leaves while another reads its partial
+}
+
 // q, k: [heads, dim] (dim even); pairs (2i, 2i+1) rotate by angle index i.
 __global__ void rope_kv_kernel(__half* __restrict__ q, const __half* __restrict__ k, const __half* __restrict__ v,
                                __half* __restrict__ kc, __half* __restrict__ vc, const __half* __restrict__ cs,
@@ -98,6 +144,16 @@ extern "C" {
 int32_t ecq_add_rmsnorm_f16(const void* h, const void* d, const void* w, void* h_out, void* y, int32_t rows,
                             int32_t n, float eps, void* stream) {
     if (!h || !w || !y || rows < 1 || n < 1 || (d && !h_out) || n > 12256) return -1;
+    if (rows == 1 && n >= 1024) {
+        // one row: spread over a cluster of CTAs instead of one CTA
+        const int chunk = (n + kRowCluster - 1) / kRowCluster;
+        const cudaError_t rc = ecq_dev::launch_pdl_cluster(
+            add_rmsnorm_row_cluster_kernel, dim3(kRowCluster), dim3(kRowThreads), (chunk + 32) * sizeof(float),
+            static_cast<cudaStream_t>(stream), kRowCluster, static_cast<const __half*>(h),
+            static_cast<const __half*>(d), static_cast<const __half*>(w), static_cast<__half*>(h_out),
+            static_cast<__half*>(y), n, eps);
+        return rc == cudaSuccess ? 0 : (cudaGetLastError(), -6);
+    }
     const int threads = n >= 1024 ? 1024 : ((n + 31) / 32) * 32;
     const cudaError_t rc = launch_pdl(add_rmsnorm_kernel, dim3(rows), dim3(threads), (n + 32) * sizeof(float),
                                       static_cast<cudaStream_t>(stream), static_cast<const __half*>(h),

@@ -90,9 +90,11 @@ class ShardedLinear:
 # ceil(tiles / warp slots) * (tile_cols / 4 + TILE_OVERHEAD); on the TP shard
 # shapes of the 7B layers and the sweep (1536..22016 rows x 512..11008 columns)
 # it picks the fastest measured width or one within 3 % of it.
-# Heads per rank up to which the split-key decode attention beats cuDNN's
-# SDPA (2049 keys, head_dim 128, in a CUDA graph).
-ECQ_ATTENTION_MAX_HEADS = 8
+# Heads per rank up to which "auto" picks the split-key decode attention. It
+# measured slower than cuDNN's SDPA at every head count from 2 to 32 (2049
+# keys, head_dim 128, CUDA graph of 32 layers: 9.2-19.1 us against 6.6-11.2
+# us), so "auto" always picks SDPA.
+ECQ_ATTENTION_MAX_HEADS = 0
 
 WARP_SLOTS = 148 * 32
 TILE_OVERHEAD = 40

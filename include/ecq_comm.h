@@ -30,13 +30,13 @@ extern "C" {
 #define ECQ_IPC_HANDLE_BYTES 64
 
 /* Exchange-buffer layout (bytes from its base): [0, 4) this rank's epoch
- * counter; [4, 8) and [8, 12) the consumer CTAs' completion and arrival
- * counters (zero between exchanges); [128, 256) up to 32 per-CTA partial sums
- * of squares (ecq_tp_add_rmsnorm_f16); [256, ...) slots[2][world][n_max],
- * u64, written by the ranks: fp32 value bits | (epoch + 1) << 32. Index
- * [e & 1] alternates with the epoch e; a slot is valid for epoch e once its
- * high half reads e + 1. The consumers run on up to 32 CTAs of 256 threads;
- * the last CTA to finish clears the counters and advances the epoch. */
+ * counter; [256, ...) slots[2][world][n_max], u64, written by the ranks:
+ * fp32 value bits | (epoch + 1) << 32. Index [e & 1] alternates with the
+ * epoch e; a slot is valid for epoch e once its high half reads e + 1. The
+ * consumers run as one thread-block cluster of 8 CTAs of 256 threads, each
+ * CTA a contiguous chunk of the elements; they combine through distributed
+ * shared memory and the cluster barrier, and rank 0 advances the epoch after
+ * every CTA has read its slots. */
 typedef struct ecq_tp_comm {
     uint32_t world;   /* ranks, 1..ECQ_TP_MAX_RANKS */
     uint32_t rank;    /* this rank */
@@ -72,7 +72,7 @@ int32_t ecq_gemv_tp(const ecq_matrix_view *m, const void *x_f16, const void *sca
  * d = sum over ranks of their values (rank order, fp32, rounded once to fp16),
  * h_out = h + d and y = rmsnorm(h_out) * w as ecq_add_rmsnorm_f16 does for
  * one row (the sum of squares is added over the CTAs' chunks in a fixed
- * order), and advance the epoch. n <= n_max, n <= 392192. After a timeout
+ * order), and advance the epoch. n <= n_max, n <= 98048. After a timeout
  * the ranks' epochs may disagree: the results are unusable and every rank
  * must rebuild its exchange buffer before the next exchange. */
 int32_t ecq_tp_add_rmsnorm_f16(const void *h, const ecq_tp_comm *comm, const void *w, void *h_out, void *y, int32_t n,

@@ -17,7 +17,9 @@ extern "C" {
 
 /* h_out = h + d (rounded to fp16; skipped when d is NULL) and
  * y = fp16(h_out * rsqrt(mean(h_out^2) + eps)) * w, for `rows` rows of n
- * (n <= 12256). */
+ * (n <= 12256): one CTA per row, or for a single row of n >= 1024 one
+ * thread-block cluster of 8 CTAs that add their partial sums of squares in
+ * rank order through distributed shared memory. h_out may be h. */
 int32_t ecq_add_rmsnorm_f16(const void *h, const void *d, const void *w, void *h_out, void *y, int32_t rows,
                             int32_t n, float eps, void *stream);
 

@@ -97,3 +97,23 @@ def test_gemv_fused_argument_errors():
                              cos_f16=16, sin_f16=16, k_cache_f16=16, v_cache_f16=16)  # odd head_dim
     assert _lib.lib().ecq_gemv_fused(m.view(), P(x), P(s), P(y), rope, P(m.workspace), m.workspace.numel(),
                                      P(m.status), st) == -1
+
+
+@pytest.mark.parametrize("rows,n,with_d", [(1, 4096, True), (1, 4096, False), (1, 11008, True), (3, 4096, True),
+                                           (1, 512, True), (1, 1031, True)])
+def test_add_rmsnorm_against_reference(rows, n, with_d):
+    # one row of n >= 1024 runs on a cluster of 8 CTAs, everything else one CTA per row
+    g = torch.Generator(device="cuda").manual_seed(rows * n)
+    h = torch.randn(rows, n, device="cuda", generator=g).half()
+    d = torch.randn(rows, n, device="cuda", generator=g).half() if with_d else None
+    w = (1 + 0.1 * torch.randn(n, device="cuda", generator=g)).half()
+    h0 = h.clone()
+    y = torch.empty_like(h)
+    assert _lib.lib().ecq_add_rmsnorm_f16(h.data_ptr(), d.data_ptr() if with_d else None, w.data_ptr(), h.data_ptr(),
+                                          y.data_ptr(), rows, n, 1e-5, torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    hr = (h0.float() + d.float()).half().float() if with_d else h0.float()
+    yr = (hr * torch.rsqrt(hr.pow(2).mean(-1, keepdim=True) + 1e-5)).half().float() * w.float()
+    if with_d:
+        assert torch.equal(h.float(), hr)  # the residual, in place
+    assert float((y.float() - yr).abs().max() / yr.abs().max()) <= 2e-3
