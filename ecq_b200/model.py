@@ -311,7 +311,9 @@ class Llama7BDecoder:
         d = None
         peer = self.xch is not None and self.use_peer
         pending = False  # the residual delta sits in the peer exchange (not in d)
+        nvtx = torch.cuda.nvtx
         for li, lw in enumerate(self.layers):
+            nvtx.range_push(f"layer {li}")  # one NVTX range per layer for timeline profilers
             if pending:
                 a = self.xch.add_rmsnorm(h, lw["ln1"], cfg.eps)
                 mk("exchange consumer: sum + add + rmsnorm")
@@ -363,6 +365,7 @@ class Llama7BDecoder:
                 if self.tp > 1:
                     d = self._all_reduce(d)
                     mk("nccl all-reduce")
+            nvtx.range_pop()
         if pending:
             a = self.xch.add_rmsnorm(h, self.norm, cfg.eps)
             mk("exchange consumer: sum + add + rmsnorm")

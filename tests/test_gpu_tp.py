@@ -1,6 +1,7 @@
 """The tensor-parallel exchange over NVLink peer memory (ecq_gemv_tp ->
-ecq_tp_add_rmsnorm_f16), on 2 GPUs: two spawned ranks, NCCL for the handle
-exchange and the comparison path. Skipped with fewer than 2 GPUs."""
+ecq_tp_add_rmsnorm_f16 / ecq_tp_sum_f16): one rank on one GPU, two ranks on
+2 GPUs, and one rank per GPU when 4 or more are visible. Spawned ranks, NCCL
+for the handle exchange and the comparison path."""
 import os
 import socket
 
@@ -13,6 +14,8 @@ pytestmark = pytest.mark.gpu
 
 # hidden 1024 = two 8x512 K-tiles, so o_proj splits over 2 ranks along whole heads
 SMALL_TP_CFG = dict(layers=2, hidden=1024, heads=8, head_dim=128, mlp=2048, vocab=1000, kv_len=64)
+# hidden 4096 and mlp 4096 = eight 8x512 K-tiles each: TP 4 and TP 8 get whole tiles and heads
+WIDE_TP_CFG = dict(layers=1, hidden=4096, heads=32, head_dim=128, mlp=4096, vocab=1000, kv_len=64)
 
 
 def _free_port():
@@ -43,6 +46,8 @@ def _worker(rank, world, port, which):
             _exchange(rank, world, dev)
         elif which == "exchange_large":
             _exchange(rank, world, dev, M=11008, n_max=11008)
+        elif which == "decoder_wide":
+            _decoder(rank, world, dev, WIDE_TP_CFG)
         else:
             _decoder(rank, world, dev)
     finally:
@@ -58,7 +63,7 @@ def _exchange(rank, world, dev, M=520, n_max=1024):
     from ecq_b200.comm import PeerExchange
     from oracle import oracle
 
-    K, g = 2048, 128
+    K, g = 512 * max(4, world), 128  # at least one 512-column K-tile per rank
     sym = syn.laplace_symbols(M, K, b=0.5, seed=61)
     sc = syn.group_scales(M, K, g, seed=62)
     enc = ecq.encode_matrix(sym, tile_cols=512, group_size=g)
@@ -98,10 +103,10 @@ def _exchange(rank, world, dev, M=520, n_max=1024):
         xch.close()
 
 
-def _decoder(rank, world, dev):
+def _decoder(rank, world, dev, cfg_kw=SMALL_TP_CFG):
     from ecq_b200.model import Llama7BConfig, Llama7BDecoder
 
-    cfg = Llama7BConfig(**SMALL_TP_CFG)
+    cfg = Llama7BConfig(**cfg_kw)
     tok = torch.tensor([17], device=dev)
     ref = Llama7BDecoder(cfg, device=dev, tp=1, seed=5)
     l_ref = ref.step_logits(tok).float()
@@ -141,9 +146,9 @@ def _decoder(rank, world, dev):
 
 @pytest.mark.parametrize("which", ["exchange", "exchange_large"])
 def test_peer_exchange_one_rank(which):
-    """One rank pushing to itself: the fused GEMV's push and both multi-CTA
-    consumers (3 CTAs for 520 rows, 32 for 11008) against the oracle over
-    several epochs, on one GPU."""
+    """One rank pushing to itself: the fused GEMV's push and both cluster
+    consumers (8 CTAs; 520 and 11008 rows) against the oracle over several
+    epochs, on one GPU."""
     import torch.multiprocessing as mp
 
     mp.spawn(_worker, args=(1, _free_port(), which), nprocs=1, join=True)
@@ -156,3 +161,14 @@ def test_peer_exchange_two_gpus(which):
     import torch.multiprocessing as mp
 
     mp.spawn(_worker, args=(2, _free_port(), which), nprocs=2, join=True)
+
+
+@pytest.mark.parametrize("which", ["exchange", "decoder_wide"])
+def test_peer_exchange_all_gpus(which):
+    """The same checks with one rank per visible GPU (4 or 8 on one box)."""
+    n = torch.cuda.device_count()
+    if n < 4:
+        pytest.skip("needs 4 or more GPUs")
+    import torch.multiprocessing as mp
+
+    mp.spawn(_worker, args=(n, _free_port(), which), nprocs=n, join=True)
