@@ -33,7 +33,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -146,57 +145,83 @@ def issue_roofline(symbols_per_s, shapes, inst_executed, sm_count, sm_mhz):
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """SM clock and clock-event (throttle) reasons of this rank's GPU during
+    the timed region, read every 2 ms on a host thread through NVML, the
+    library nvidia-smi queries (read-only calls). The timed regions last
+    tens of milliseconds, shorter than nvidia-smi's sampling start-up."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    def __init__(self, device, period_s: float = 0.002):
+        self.device = device
+        self.period = period_s
+        self.samples: list = []
+        self.max_mhz = None
+        self.nvml = None
+        self.handle = None
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
+    def _open(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        self.nvml = pynvml
+        prop = torch.cuda.get_device_properties(self.device)
+        try:
+            bus = f"{prop.pci_domain_id:08X}:{prop.pci_bus_id:02X}:{prop.pci_device_id:02X}.0"
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+
+    def _run(self):
+        nv, h = self.nvml, self.handle
+        reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while True:
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), reasons(h)))
+            except Exception:
+                return
+            if self.stop.wait(self.period):
+                return
 
     def __enter__(self):
+        import threading
+
+        self.stop = threading.Event()
+        self.thread = None
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "50", "-i", str(self.gpu)], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
+            self._open()
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
         except Exception:
-            self.proc = None
-        time.sleep(0.15)
+            self.handle = None
         return self
 
     def __exit__(self, *a):
-        self.lines = []
-        if self.proc is not None:
-            time.sleep(0.1)
-            self.proc.terminate()
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+        if self.nvml is not None:
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.nvml.nvmlShutdown()
             except Exception:
-                self.proc.kill()
-                out = ""
-            self.lines = [l for l in out.splitlines() if l.strip()]
+                pass
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
-            f = [v.strip() for v in l.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        nv = self.nvml
+        masks = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+                 "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+                 "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+                 "sw_power_cap": "nvmlClocksEventReasonSwPowerCap"}
+        reasons = set()
+        for name, attr in masks.items():
+            bit = getattr(nv, attr, None)
+            if bit is not None and any(r & bit for _, r in self.samples):
+                reasons.add(name)
+        return {"sm_mhz": statistics.median(c for c, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(self.samples), "source": "NVML every 2 ms"}
 
 
 def cpu_baseline(inputs, threads, repeats=2, min_seconds=0.0):
@@ -399,7 +424,7 @@ def run_ecq(args):
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev) as clocks:
         with torch.cuda.stream(stream):
             ev0.record(stream)
             for _ in range(args.steps):
