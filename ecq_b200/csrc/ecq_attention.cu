@@ -212,10 +212,12 @@ int64_t ecq_decode_attention_workspace_bytes(int32_t heads, int32_t splits) {
 
 int32_t ecq_decode_attention_splits(int32_t heads, int32_t keys) {
     if (heads < 1 || keys < 1) return -1;
-    // about two CTAs per SM over all heads, and at least 32 keys per split
+    // about two CTAs per SM over all heads, at least 32 keys per split, and
+    // no more splits than the merge handles
     int s = (2 * ecq_dev::sm_count_cached() + heads - 1) / heads;
     const int max_s = (keys + 31) / 32;
     if (s > max_s) s = max_s;
+    if (s > kMaxSplits) s = kMaxSplits;
     return s < 1 ? 1 : s;
 }
 

@@ -287,9 +287,8 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
     const uint32_t c0 = kt * (MPL * 32);
     const uint32_t len = p.stream_len[t * 32 + lane];
 
-    uint32_t a = buf + lane;  // shared-window address
-    uint32_t x = (lds_u8(a) << 24) | (lds_u8(a + 32) << 16) | (lds_u8(a + 64) << 8) | lds_u8(a + 96);
-    a += 128;
+    uint32_t x, a, b0, b1;  // rANS state, next stream byte's shared-window address, read-ahead bytes
+    stream_cursor_init(buf, lane, x, a, b0, b1);
     const uint32_t cent = ((p.flags >> ECQ_FLAG_CONSTANT_SYM_SHIFT) & 15u) << 14;  // constant table: sym field
 
     constexpr bool GEMV = MODE == kModeGemv;
@@ -348,8 +347,8 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
 #pragma unroll
                 for (int mm = 0; mm < GPL; mm += 2) {
                     const int m = sg * GPL + mm;
-                    const uint32_t e0 = decode_step(x, a, tb);
-                    const uint32_t e1 = decode_step(x, a, tb);
+                    const uint32_t e0 = decode_step(x, a, b0, b1, tb);
+                    const uint32_t e1 = decode_step(x, a, b0, b1, tb);
                     const uint64_t w2 = add2(pack2(entry_weight_bits(e0), entry_weight_bits(e1)), kNegBias2);
                     part2 = fma2(w2, pack2(__float_as_uint(xs[m]), __float_as_uint(xs[m + 1])), part2);
                 }
@@ -367,7 +366,7 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
                     if constexpr (CONSTANT) {
                         e = cent;
                     } else {
-                        e = decode_step(x, a, tb);
+                        e = decode_step(x, a, b0, b1, tb);
                     }
                     const size_t idx = static_cast<size_t>(r0 + r) * p.cols + c0 + 32 * m + lane;
                     if constexpr (GEMV) {
@@ -505,9 +504,8 @@ __device__ __forceinline__ void process_tile_batch(const MatrixParams& p, uint32
     const uint32_t c0 = kt * (MPL * 32);
     const uint32_t len = p.stream_len[t * 32 + lane];
 
-    uint32_t a = buf + lane;
-    uint32_t x = (lds_u8(a) << 24) | (lds_u8(a + 32) << 16) | (lds_u8(a + 64) << 8) | lds_u8(a + 96);
-    a += 128;
+    uint32_t x, a, b0, b1;  // rANS state, next stream byte's shared-window address, read-ahead bytes
+    stream_cursor_init(buf, lane, x, a, b0, b1);
     const uint32_t cent = ((p.flags >> ECQ_FLAG_CONSTANT_SYM_SHIFT) & 15u) << 14;
 
     constexpr int NSR = (kTileRows * NSG + 31) / 32;
@@ -548,7 +546,7 @@ __device__ __forceinline__ void process_tile_batch(const MatrixParams& p, uint32
                 if constexpr (CONSTANT) {
                     e = cent;
                 } else {
-                    e = decode_step(x, a, tb);
+                    e = decode_step(x, a, b0, b1, tb);
                 }
                 // the sym field ORed into the mantissa of 64.0f is 64 + s/8
                 const float wf = __uint_as_float((e & 0x3C000u) | 0x42800000u) - 65.0f;  // (s - 8) / 8, exact

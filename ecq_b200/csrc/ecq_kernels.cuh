@@ -114,47 +114,70 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
 }
 
 // One decode step for this lane. tb is the shared-window address of the
-// packed decode table, a that of the lane's next stream byte (byte p of lane
-// j of a tile at tile_base + 32p + j). Returns the table entry.
+// packed decode table, a that of the lane's next unread stream byte (byte p
+// of lane j of a tile at tile_base + 32p + j), and b0, b1 the bytes at a and
+// a + 32, loaded ahead (stream_cursor_init sets them up). Returns the table
+// entry.
 //
-// Renormalisation reads the next two bytes ahead of need and shifts in 0, 1
-// or 2 of them with one funnel shift. After a decode step of an intact
-// stream 2^9 <= x < 2^31, and the reference's byte loop reads one byte iff
-// x < 2^23 and a second iff x < 2^15: the shift is clz(2x) & 24 bits
-// (clz(2x) = clz(x) - 1 lies in [0,7], [8,15] or [16,21] for the three
-// cases). A damaged stream can leave x below 2^9; the shift is then at most
-// 24 bits (3 bytes, the read-ahead bound the callers pad for), the state is
-// wrong from there on, and the end-of-stream check flags the tile.
-__device__ __forceinline__ uint32_t decode_step(uint32_t& x, uint32_t& a, uint32_t tb) {
+// Renormalisation shifts in 0, 1 or 2 of the read-ahead bytes with one
+// funnel shift. After a decode step of an intact stream 2^9 <= x < 2^31,
+// and the reference's byte loop reads one byte iff x < 2^23 and a second iff
+// x < 2^15: the shift is clz(2x) & 24 bits (clz(2x) = clz(x) - 1 lies in
+// [0,7], [8,15] or [16,21] for the three cases). A damaged stream can leave
+// x below 2^9; the shift is then at most 24 bits (3 bytes, the read-ahead
+// bound the callers pad for), the state is wrong from there on, and the
+// end-of-stream check flags the tile.
+//
+// Only lanes that shifted bytes in reload b0 and b1 (predicated loads at the
+// new a): most steps consume no byte, and a lane whose load is predicated
+// off takes no part in the shared-memory access, so the two byte loads cost
+// far fewer bank wavefronts than loads by every lane. The reload is issued
+// at the end of the step and consumed by the next step's funnel shift, after
+// that step's table lookup, so its latency stays off the decode chain.
+__device__ __forceinline__ uint32_t decode_step(uint32_t& x, uint32_t& a, uint32_t& b0, uint32_t& b1, uint32_t tb) {
     uint32_t e;
     asm volatile(
         "{\n\t"
-        ".reg .u32 b0, b1, sl, q, f, bi, nx, sh;\n\t"
-        "ld.shared.u8 b0, [%1];\n\t"          // next two stream bytes, read ahead of need
-        "ld.shared.u8 b1, [%1+32];\n\t"
+        ".reg .u32 sl, q, f, bi, nx, sh;\n\t"
+        ".reg .pred rl;\n\t"
         "and.b32 sl, %0, 16383;\n\t"          // slot
-        "mad.lo.u32 sl, sl, 4, %3;\n\t"
+        "mad.lo.u32 sl, sl, 4, %5;\n\t"
         "ld.shared.u32 %2, [sl];\n\t"         // e = table[slot]
         "shr.u32 q, %0, 14;\n\t"
         "shr.u32 f, %2, 18;\n\t"
         "and.b32 bi, %2, 16383;\n\t"
         "mad.lo.u32 %0, f, q, bi;\n\t"        // x = freq * (x >> 14) + slot - cumfreq
-        "prmt.b32 nx, b1, b0, 0x4011;\n\t"    // b0 << 24 | b1 << 16
+        "prmt.b32 nx, %4, %3, 0x4011;\n\t"    // b0 << 24 | b1 << 16
         "shl.b32 sh, %0, 1;\n\t"             // x < 2^31 here, so clz(2x) = clz(x) - 1
         "clz.b32 sh, sh;\n\t"
         "and.b32 sh, sh, 24;\n\t"           // 0, 8 or 16: x >= 2^23, >= 2^15, < 2^15
         "shf.l.wrap.b32 %0, nx, %0, sh;\n\t"  // x = (x << sh) | (nx >> (32 - sh))
         "mad.lo.u32 %1, sh, 4, %1;\n\t"       // 32 bytes per consumed byte
+        "setp.ne.u32 rl, sh, 0;\n\t"
+        "@rl ld.shared.u8 %3, [%1];\n\t"      // refill the read-ahead bytes
+        "@rl ld.shared.u8 %4, [%1+32];\n\t"
         "}"
-        : "+r"(x), "+r"(a), "=r"(e)
+        : "+r"(x), "+r"(a), "=r"(e), "+r"(b0), "+r"(b1)
         : "r"(tb));
     return e;
+}
+
+// Start decoding the lane's stream of a tile staged at shared address buf:
+// the 4-byte initial state (big-endian, 32 bytes apart), then the two
+// read-ahead bytes decode_step expects.
+__device__ __forceinline__ void stream_cursor_init(uint32_t buf, int lane, uint32_t& x, uint32_t& a, uint32_t& b0,
+                                                   uint32_t& b1) {
+    a = buf + lane;
+    x = (lds_u8(a) << 24) | (lds_u8(a + 32) << 16) | (lds_u8(a + 64) << 8) | lds_u8(a + 96);
+    a += 128;
+    b0 = lds_u8(a);
+    b1 = lds_u8(a + 32);
 }
 
 template <int MPL>
 __host__ __device__ constexpr uint32_t overrun_pad() {
     // a lane reads at most 4 + 3 bytes per symbol of a tile, 32 lanes apart,
-    // plus one byte row of read-ahead
+    // plus one byte row of read-ahead (the refill after its last step)
     return (32u * (5u + 3u * kTileRows * MPL) + 127u) & ~127u;
 }
 

@@ -165,9 +165,8 @@ __device__ __forceinline__ bool decode_tile_to_w(const MatmulParams& p, uint32_t
     const int rows_here = static_cast<int>(min(static_cast<uint32_t>(kTileRows), p.rows - r0));
     const uint32_t c0 = kt * (MPL * 32);
     const uint32_t len = p.stream_len[t * 32 + lane];
-    uint32_t a = buf + lane;
-    uint32_t x = (lds_u8(a) << 24) | (lds_u8(a + 32) << 16) | (lds_u8(a + 64) << 8) | lds_u8(a + 96);
-    a += 128;
+    uint32_t x, a, b0, b1;  // rANS state, next stream byte's shared-window address, read-ahead bytes
+    stream_cursor_init(buf, lane, x, a, b0, b1);
     const uint32_t cent = ((p.flags >> ECQ_FLAG_CONSTANT_SYM_SHIFT) & 15u) << 14;
     // lane l < NSG loads the scale of the tile row's group l; its column index is fixed per tile
     const __half* srow = p.scales + static_cast<size_t>(r0) * p.ng + (c0 + (lane < NSG ? lane : 0) * GPL * 32) / p.group_size;
@@ -194,8 +193,8 @@ __device__ __forceinline__ bool decode_tile_to_w(const MatmulParams& p, uint32_t
             if constexpr (CONSTANT) {
                 e0 = e1 = cent;
             } else {
-                e0 = decode_step(x, a, tb);
-                e1 = decode_step(x, a, tb);
+                e0 = decode_step(x, a, b0, b1, tb);
+                e1 = decode_step(x, a, b0, b1, tb);
             }
             // (sym - 8) * scale = (2^23 + sym*2^14) * g - (2^23 + 8*2^14) * g, exact in fp32; one rounding to fp16
             const int s0 = (2 * q) / GPL, s1 = (2 * q + 1) / GPL;  // compile-time once unrolled

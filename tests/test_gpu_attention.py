@@ -29,7 +29,7 @@ def _attention(q, k, v, splits=None):
     return out, ws
 
 
-@pytest.mark.parametrize("H,T", [(4, 2049), (32, 2049), (1, 1), (8, 7), (4, 65), (2, 4097), (16, 300)])
+@pytest.mark.parametrize("H,T", [(4, 2049), (32, 2049), (1, 1), (8, 7), (4, 65), (2, 4097), (1, 8193), (16, 300)])
 def test_decode_attention_matches_reference(H, T):
     D = 128
     g = torch.Generator(device="cuda").manual_seed(H * 1000 + T)
