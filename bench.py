@@ -882,12 +882,15 @@ def run_batched(dev, world=1, rank=0, barrier=None):
         m.ensure_workspace(min(B, 8))
         m512.ensure_workspace(min(B, 8))
         ms = timed(lambda: reduce(m.matmul(x, sc)))
-        from ecq_b200.device import GEMV_MAX_BATCH
+        from ecq_b200.device import GEMV_MAX_BATCH, TENSOR_CORE_MAX_BATCH
 
         path = ("fused GEMV" if B == 1 else
                 "fused GEMV, each tile decoded once for the batch" if B <= GEMV_MAX_BATCH else
-                "fused decode + tcgen05 MMA (x in TMEM, W tile in SMEM)")
+                "fused decode + tcgen05 MMA (x in TMEM, W tile in SMEM)" if B <= TENSOR_CORE_MAX_BATCH else
+                "W decoded once to fp16 (matrix_kernel) + cuBLAS GEMM")
         row = row_of(B, ms, path + " [8x256 tiles]")
+        if B > TENSOR_CORE_MAX_BATCH:
+            row["tcgen05_ms"] = round(timed(lambda: reduce(m.matmul_tc(x, sc))), 4)
         if B > 1:
             row["control_decode_fp16_cublas_ms"] = round(
                 timed(lambda: reduce(torch.mm(x, m.dequantize(sc).t(), out_dtype=torch.float32).to(torch.float16))), 4)

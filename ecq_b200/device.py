@@ -35,6 +35,12 @@ def _require_cuda(t: torch.Tensor, name: str) -> None:
 # the GEMV's CUDA-core math for 8 tokens costs 2x its single-token time, more
 # than the tcgen05 kernel (1.3x) or decoding W to fp16 once for cuBLAS (1.35x).
 GEMV_MAX_BATCH = 4
+# Token batches above GEMV_MAX_BATCH and up to this size run the tcgen05 kernel;
+# larger ones decode W once to fp16 for cuBLAS. Measured on 28672 x 8192 (8x256
+# tiles): the two are level at 32 tokens and the decode-once path is 12 % faster
+# at 128, where re-reading x for every weight item costs the tcgen05 kernel more
+# than it saves by never writing W.
+TENSOR_CORE_MAX_BATCH = 32
 
 
 @dataclass
@@ -164,18 +170,20 @@ class DeviceMatrix:
                                self.mm_workspace.numel(), ptr(self.status), _stream_ptr(stream)), "matmul")
         return out
 
-    def matmul(self, x: torch.Tensor, scales: torch.Tensor, fused_max_batch: int = GEMV_MAX_BATCH) -> torch.Tensor:
+    def matmul(self, x: torch.Tensor, scales: torch.Tensor, fused_max_batch: int = GEMV_MAX_BATCH,
+               tensor_core_max_batch: int = TENSOR_CORE_MAX_BATCH) -> torch.Tensor:
         """y = x @ W^T for x [..., cols] fp16: the one dispatch every batched
         entry point uses. Up to `fused_max_batch` token rows run the fused
-        GEMV, which decodes each tile once for the whole batch. Larger batches
-        run the tcgen05 kernel (matmul_tc) when the tile layout has one (tile
-        widths 128 and 256); otherwise W is decoded once to fp16
-        (dequantize) for a tensor-core GEMM."""
+        GEMV, which decodes each tile once for the whole batch. Batches up to
+        `tensor_core_max_batch` run the tcgen05 kernel (matmul_tc) when the
+        tile layout has one (tile widths 128 and 256); otherwise, and for
+        larger batches, W is decoded once to fp16 (dequantize) for a
+        tensor-core GEMM."""
         lead = x.shape[:-1]
         x2 = x.reshape(-1, self.cols)
         if x2.shape[0] <= fused_max_batch:
             y = self.gemv(x2.contiguous(), scales)
-        elif self.tensor_core_ok():
+        elif x2.shape[0] <= tensor_core_max_batch and self.tensor_core_ok():
             y = self.matmul_tc(x2, scales)
         else:
             w = self.dequantize(scales)

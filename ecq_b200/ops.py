@@ -18,7 +18,7 @@ import torch
 from . import _lib
 from ._lib import MatrixView, check, lib
 from .codec import RANSTable, encode_matrix
-from .device import GEMV_MAX_BATCH, DeviceMatrix, Packed4Matrix
+from .device import GEMV_MAX_BATCH, TENSOR_CORE_MAX_BATCH, DeviceMatrix, Packed4Matrix
 from .synthetic import quantize_symmetric_groups
 
 
@@ -95,12 +95,12 @@ def _(x, data, tile_offset, stream_len, dec_table, scales, workspace, status, ro
 def rans_matmul(x: torch.Tensor, m: DeviceMatrix, scales: torch.Tensor) -> torch.Tensor:
     """x [B, cols] fp16 -> y [B, rows], routed as DeviceMatrix.matmul routes:
     up to GEMV_MAX_BATCH tokens the fused GEMV (each tile decoded once for the
-    batch), more the tcgen05 kernel when the tile layout has one, else
-    W decoded once to fp16 for a tensor-core GEMM."""
+    batch), up to TENSOR_CORE_MAX_BATCH the tcgen05 kernel when the tile
+    layout has one, else W decoded once to fp16 for a tensor-core GEMM."""
     x2 = x.reshape(-1, m.cols)
     if x2.shape[0] <= GEMV_MAX_BATCH:
         return rans_gemv(x2.contiguous(), m, scales)
-    if not m.tensor_core_ok():
+    if x2.shape[0] > TENSOR_CORE_MAX_BATCH or not m.tensor_core_ok():
         w = m.dequantize(scales)
         return torch.mm(x2.contiguous(), w.t(), out_dtype=torch.float32).to(torch.float16)
     need = int(lib().ecq_matmul_workspace_bytes(m.view(), x2.shape[0]))
