@@ -248,13 +248,7 @@ __device__ __forceinline__ void complete_pending(const MatrixParams& p, PendingS
 __device__ __forceinline__ void finish_tile(const MatrixParams& p, uint32_t t, float (&acc)[8], int rows_here,
                                             int lane, PendingSlab& pend) {
     complete_pending(p, pend, lane);
-    // short slab: move row 0 to acc[0]
-#pragma unroll 1
-    for (int r = rows_here; r < kTileRows; ++r) {
-#pragma unroll
-        for (int k = 0; k < kTileRows - 1; ++k) acc[k] = acc[k + 1];
-        acc[kTileRows - 1] = 0.f;
-    }
+    // rows past a short slab's end hold 0
     const float v = transpose_reduce8(acc, lane);
     // lane 4*b2 + 8*b3 + 16*b4 holds row 4*b4 + 2*b3 + b2
     float rv[kTileRows];
@@ -323,9 +317,19 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
 #pragma unroll
         for (int r = 0; r < kTileRows; ++r) acc[r] = 0.f;
     }
+    // x pairs packed once per tile for the f32x2 multiply-add of the row loop
+    constexpr bool PAIRS = GEMV && !CONSTANT && (GPL % 2 == 0);
+    uint64_t xp[PAIRS ? MPL / 2 : 1];
+    if constexpr (PAIRS) {
+#pragma unroll
+        for (int i = 0; i < MPL / 2; ++i) xp[i] = pack2(__float_as_uint(xs[2 * i]), __float_as_uint(xs[2 * i + 1]));
+    }
 
-#pragma unroll 1
-    for (int r = 0; r < rows_here; ++r) {
+    // the row loop is unrolled: a static row index, so a GEMV row's sum lands in
+    // acc[r] with no register shuffling, and rows overlap in the schedule
+#pragma unroll
+    for (int r = 0; r < kTileRows; ++r) {
+        if (r >= rows_here) break;
         float rowacc = 0.f;
         float sreg = 0.f;  // the register of sca holding row r's scales
         if constexpr (SCALED) {
@@ -341,7 +345,7 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
 #pragma unroll
         for (int sg = 0; sg < NSG; ++sg) {
             float part = 0.f;
-            if constexpr (GEMV && !CONSTANT && (GPL % 2 == 0)) {
+            if constexpr (PAIRS) {
                 // two symbols per packed f32x2 add + fma
                 uint64_t part2 = 0;
 #pragma unroll
@@ -350,7 +354,7 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
                     const uint32_t e0 = decode_step(x, a, b0, b1, tb);
                     const uint32_t e1 = decode_step(x, a, b0, b1, tb);
                     const uint64_t w2 = add2(pack2(entry_weight_bits(e0), entry_weight_bits(e1)), kNegBias2);
-                    part2 = fma2(w2, pack2(__float_as_uint(xs[m]), __float_as_uint(xs[m + 1])), part2);
+                    part2 = fma2(w2, xp[m / 2], part2);
                 }
                 float lo, hi;
                 unpack2(part2, lo, hi);
@@ -386,11 +390,7 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
             }
             if constexpr (GEMV) rowacc = fmaf(__shfl_sync(0xffffffffu, sreg, (r * NSG + sg) & 31), part, rowacc);
         }
-        if constexpr (GEMV) {
-#pragma unroll
-            for (int k = 0; k < kTileRows - 1; ++k) acc[k] = acc[k + 1];
-            acc[kTileRows - 1] = rowacc;
-        }
+        if constexpr (GEMV) acc[r] = rowacc;
     }
     if constexpr (!CONSTANT) {
         if (x != kL || (a - buf - lane) != len * 32u) atomicOr(p.status, ECQ_STATUS_CORRUPT);

@@ -25,3 +25,25 @@ def test_rans_matmul_fake_shapes():
                                   t(16384, torch.int32), torch.empty(1024, 16, dtype=torch.float16, device=meta),
                                   t(10, torch.uint8), t(1, torch.int32), 1024, 2048, 8, 256, 128, 0, 700)
     assert y.shape == (24, 1024) and y.dtype == torch.float16 and y.device == meta
+
+
+@pytest.mark.parametrize("B,tc_ok,want", [(1, True, "gemv"), (4, True, "gemv"), (5, True, "tc"), (32, True, "tc"),
+                                          (33, True, "dequant"), (128, True, "dequant"), (8, False, "dequant")])
+def test_matmul_dispatch_by_batch(B, tc_ok, want, monkeypatch):
+    """DeviceMatrix.matmul routes by token count: the fused GEMV up to
+    GEMV_MAX_BATCH, the tcgen05 kernel up to TENSOR_CORE_MAX_BATCH when the
+    tile layout has one, else W decoded once for a dense GEMM."""
+    from ecq_b200.device import DeviceMatrix
+
+    m = object.__new__(DeviceMatrix)
+    m.rows, m.cols = 16, 32
+    called = []
+    monkeypatch.setattr(DeviceMatrix, "tensor_core_ok", lambda self: tc_ok)
+    monkeypatch.setattr(DeviceMatrix, "gemv",
+                        lambda self, x, s: called.append("gemv") or x.new_empty(x.shape[0], 16))
+    monkeypatch.setattr(DeviceMatrix, "matmul_tc",
+                        lambda self, x, s: called.append("tc") or x.new_empty(x.shape[0], 16))
+    monkeypatch.setattr(DeviceMatrix, "dequantize",
+                        lambda self, s: called.append("dequant") or torch.empty(16, 32, dtype=torch.float16, device="meta"))
+    y = m.matmul(torch.empty(B, 32, dtype=torch.float16, device="meta"), None)
+    assert called == [want] and y.shape == (B, 16)
