@@ -245,8 +245,8 @@ __device__ __forceinline__ void complete_pending(const MatrixParams& p, PendingS
     pend.slab = 0xffffffffu;
 }
 
-__device__ __forceinline__ void finish_tile(const MatrixParams& p, uint32_t t, float (&acc)[8], int rows_here,
-                                            int lane, PendingSlab& pend) {
+__device__ __forceinline__ void finish_tile(const MatrixParams& p, uint32_t t, uint32_t slab, float (&acc)[8],
+                                            int rows_here, int lane, PendingSlab& pend) {
     complete_pending(p, pend, lane);
     // rows past a short slab's end hold 0
     const float v = transpose_reduce8(acc, lane);
@@ -255,7 +255,6 @@ __device__ __forceinline__ void finish_tile(const MatrixParams& p, uint32_t t, f
 #pragma unroll
     for (int r = 0; r < kTileRows; ++r)
         rv[r] = __shfl_sync(0xffffffffu, v, ((r >> 2) & 1) * 16 + ((r >> 1) & 1) * 8 + (r & 1) * 4);
-    const uint32_t slab = t / p.n_ktiles;
     uint32_t old = 0;
     if (lane == 0) {
         float4* dst = reinterpret_cast<float4*>(p.partials + static_cast<size_t>(t) * kTileRows);
@@ -271,11 +270,9 @@ __device__ __forceinline__ void finish_tile(const MatrixParams& p, uint32_t t, f
 // Decode one tile (buf = offset of its bytes in shared memory) and either
 // accumulate its GEMV contribution or store its symbols.
 template <int MPL, int GPL, int MODE, bool CONSTANT>
-__device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, uint32_t buf, uint32_t tb,
-                                             int lane, PendingSlab& pend) {
+__device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, uint32_t slab, uint32_t kt,
+                                             uint32_t buf, uint32_t tb, int lane, PendingSlab& pend) {
     constexpr int NSG = MPL / GPL;  // scale groups per tile row
-    const uint32_t slab = t / p.n_ktiles;
-    const uint32_t kt = t - slab * p.n_ktiles;
     const uint32_t r0 = slab * kTileRows;
     const int rows_here = static_cast<int>(min(static_cast<uint32_t>(kTileRows), p.rows - r0));
     const uint32_t c0 = kt * (MPL * 32);
@@ -398,7 +395,7 @@ __device__ __forceinline__ void process_tile(const MatrixParams& p, uint32_t t, 
         if (len != 4u) atomicOr(p.status, ECQ_STATUS_CORRUPT);
     }
 
-    if constexpr (GEMV) finish_tile(p, t, acc, rows_here, lane, pend);
+    if constexpr (GEMV) finish_tile(p, t, slab, acc, rows_here, lane, pend);
 }
 
 // Reduce v[0..N) (N = 2, 4 or 8) over the 32 lanes in a fixed order. Lane l
@@ -493,12 +490,11 @@ __device__ __forceinline__ void complete_pending_batch(const MatrixParams& p, Pe
 // the GPL symbols a lane holds of one scale group, then in fp32 with the
 // group scale; per row, a fixed-order warp reduction of the NB sums.
 template <int MPL, int GPL, int NB, bool CONSTANT>
-__device__ __forceinline__ void process_tile_batch(const MatrixParams& p, uint32_t t, uint32_t buf, uint32_t tb,
-                                                   uint32_t xsb, int lane, PendingSlab& pend) {
+__device__ __forceinline__ void process_tile_batch(const MatrixParams& p, uint32_t t, uint32_t slab, uint32_t kt,
+                                                   uint32_t buf, uint32_t tb, uint32_t xsb, int lane,
+                                                   PendingSlab& pend) {
     constexpr int NSG = MPL / GPL;
     constexpr int NH = NB / 2;
-    const uint32_t slab = t / p.n_ktiles;
-    const uint32_t kt = t - slab * p.n_ktiles;
     const uint32_t r0 = slab * kTileRows;
     const int rows_here = static_cast<int>(min(static_cast<uint32_t>(kTileRows), p.rows - r0));
     const uint32_t c0 = kt * (MPL * 32);
@@ -666,6 +662,9 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
 
     uint32_t phase0 = 0, phase1 = 0;
     PendingSlab pend{0xffffffffu, 0u, 0};
+    // the run's tiles are consecutive: one division for the first tile's
+    // (slab, k-tile), then a carry per tile
+    uint32_t slab = t_begin / p.n_ktiles, kt = t_begin - slab * p.n_ktiles;
     for (uint32_t t = t_begin; ok && t < t_end; ++t) {
         const int stage = (t - t_begin) & 1;
         if (t + 1 < t_end) {
@@ -686,14 +685,18 @@ __global__ void __launch_bounds__(1024, 1) matrix_kernel(MatrixParams p) {
         asm volatile("" : "+r"(buf)::"memory");  // keep this tile's byte loads after its wait
         if constexpr (BATCH) {
             if (constant)
-                process_tile_batch<MPL, GPL, NB, true>(p, t, buf, sbase, sbase + kTableBytes, lane, pend);
+                process_tile_batch<MPL, GPL, NB, true>(p, t, slab, kt, buf, sbase, sbase + kTableBytes, lane, pend);
             else
-                process_tile_batch<MPL, GPL, NB, false>(p, t, buf, sbase, sbase + kTableBytes, lane, pend);
+                process_tile_batch<MPL, GPL, NB, false>(p, t, slab, kt, buf, sbase, sbase + kTableBytes, lane, pend);
         } else {
             if (constant)
-                process_tile<MPL, GPL, MODE, true>(p, t, buf, sbase, lane, pend);
+                process_tile<MPL, GPL, MODE, true>(p, t, slab, kt, buf, sbase, lane, pend);
             else
-                process_tile<MPL, GPL, MODE, false>(p, t, buf, sbase, lane, pend);
+                process_tile<MPL, GPL, MODE, false>(p, t, slab, kt, buf, sbase, lane, pend);
+        }
+        if (++kt == p.n_ktiles) {
+            kt = 0;
+            ++slab;
         }
     }
     if constexpr (GEMV) complete_pending(p, pend, lane);

@@ -176,8 +176,9 @@ __device__ __forceinline__ bool decode_tile_to_w(const MatmulParams& p, uint32_t
     uint32_t hold[NP];
 #pragma unroll
     for (int q = 0; q < NP; ++q) hold[q] = 0u;
-#pragma unroll 1
-    for (int r = 0; r < rows_here; ++r) {
+#pragma unroll
+    for (int r = 0; r < kTileRows; ++r) {
+        if (r >= rows_here) break;
         float sn = 0.f;
         if (lane < NSG && r + 1 < rows_here) sn = __half2float(srow[static_cast<size_t>(r + 1) * p.ng]) * 6.103515625e-05f;
         float g[NSG], nb[NSG];
