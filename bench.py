@@ -898,9 +898,12 @@ def run_batched(dev, world=1, rank=0, barrier=None):
             row["gemv_8x512_ms"] = round(timed(lambda: reduce(m512.gemv(x, sc))), 4)
         if B == 8:
             row["gemv_8x256_batched_ms"] = round(timed(lambda: reduce(m.gemv(x, sc))), 4)
+            # the dispatch on the default GEMV encoding (8x512: no tcgen05 kernel)
+            row["dispatch_8x512_ms"] = round(timed(lambda: reduce(m512.matmul(x, sc))), 4)
         out["batches"][str(B)] = row
     b1, b8 = out["batches"]["1"], out["batches"]["8"]
     out["b8_over_b1_time_8x512"] = round(b8["gemv_8x512_ms"] / b1["gemv_8x512_ms"], 3)
+    out["b8_dispatch_over_b1_time_8x512"] = round(b8["dispatch_8x512_ms"] / b1["gemv_8x512_ms"], 3)
     m.check()
     m512.check()
     return out
