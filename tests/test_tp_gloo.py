@@ -148,3 +148,22 @@ def test_shard_tile_widths():
     for rows, cols in ((8, 128), (1000, 384), (4096, 1408)):
         c = shard_tile_cols(rows, cols)
         assert cols % c == 0 and c % 128 == 0 or c == 128
+
+
+# Fastest tile width per shard shape, measured on one B200 (graph of 24 GEMV
+# launches per width, Laplace b = 0.5, group 128); 11008x4096 is a tie within
+# 0.3 % (8x512 46.7 us, 8x256 46.6 us), so either width passes there.
+MEASURED_BEST_TILE = {
+    (1536, 4096): (256,), (2752, 4096): (512,), (3072, 4096): (512,), (4096, 512): (128,),
+    (4096, 1024): (128,), (4096, 1408): (128,), (4096, 2048): (256,), (4096, 2816): (256,),
+    (4096, 4096): (512,), (4096, 5504): (128,), (4096, 11008): (256,), (5504, 4096): (256,),
+    (6144, 4096): (256,), (11008, 512): (256,), (11008, 1024): (512,), (11008, 2048): (256,),
+    (11008, 4096): (512, 256), (12288, 4096): (512,), (22016, 4096): (512,),
+}
+
+
+@pytest.mark.parametrize("shape", sorted(MEASURED_BEST_TILE))
+def test_shard_tile_model_matches_measured_best(shape):
+    from ecq_b200.model import shard_tile_cols
+
+    assert shard_tile_cols(*shape) in MEASURED_BEST_TILE[shape]
