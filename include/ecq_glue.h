@@ -43,7 +43,8 @@ int32_t ecq_silu_mul_f16(const void *gate_up, void *m, int32_t f, int32_t rows, 
  * v_cache). head_dim must be 128; pointers 8-byte aligned. The workspace
  * (ecq_decode_attention_workspace_bytes) must be zero-filled once; each call
  * leaves its counters zero again. ecq_decode_attention_splits gives a split
- * count that puts about two CTAs per SM. */
+ * count that puts about two CTAs per SM, at least 32 keys per split and at
+ * most 128 splits (the merge's limit; more returns ECQ_ERR_ARG). */
 int64_t ecq_decode_attention_workspace_bytes(int32_t heads, int32_t splits);
 int32_t ecq_decode_attention_splits(int32_t heads, int32_t keys);
 int32_t ecq_decode_attention_f16(const void *q, const void *k_cache, const void *v_cache, void *out, int32_t heads,
